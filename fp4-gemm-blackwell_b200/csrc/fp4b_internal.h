@@ -1,0 +1,53 @@
+// fp4b_internal.h -- host-side interfaces between the kernels and the C ABI.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace fp4b {
+
+// A BF16 matrix [rows, cols] with row stride `ld` elements, quantized into a
+// zero-padded NVFP4 operand [rows_pad, k_pad/2] + interleaved scales
+// (rows_pad * k_pad / 16 bytes).  rows_pad, k_pad: multiples of 128.
+struct QuantizeArgs {
+    const void* src;
+    long rows, cols, ld;
+    long rows_pad, k_pad;
+    uint8_t* fp4;
+    uint8_t* sf;
+};
+
+// Check the geometry; returns nullptr when valid, else a message.
+const char* quantize_check(const QuantizeArgs& a);
+cudaError_t quantize_launch(const QuantizeArgs& a, cudaStream_t stream);
+
+// D[M, n_out] = epilogue(A_fp4 x B_fp4^T): alpha * acc + beta * C, rounded to
+// bf16, then + bias[n] rounded to bf16 again (bias optional).  A has
+// m_rows_pad rows, B has n_rows_pad rows, both k_pad wide (multiples of 128).
+struct GemmArgs {
+    const uint8_t* a_fp4;
+    const uint8_t* a_sf;
+    const uint8_t* b_fp4;
+    const uint8_t* b_sf;
+    long m, n_out, k_pad;
+    long m_rows_pad, n_rows_pad;
+    const void* c;  // bf16 [m, ldc] or null
+    long ldc;
+    void* d;        // bf16 [m, ldd]
+    long ldd;
+    const void* bias;  // bf16 [n_out] or null
+    float alpha, beta;
+};
+
+const char* gemm_check(const GemmArgs& g);
+cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream);
+
+// Device-side error word written by kernels that gave up on a bounded wait.
+int* device_error_word();
+int read_and_clear_device_error();
+
+// Per-thread message of the last failure in the C ABI.
+void set_last_error(const char* fmt, ...);
+
+}  // namespace fp4b

@@ -1,0 +1,502 @@
+"""
+NVFP4 linear layers on B200 (sm_100a) -- drop-in for the ``fp4_gemm`` module
+of VincentKaufmann/fp4-gemm-blackwell (fp4_gemm.py in that project).
+
+Same public names, argument meaning, return values and errors:
+
+    fp4_matmul(A, B, C=None, alpha=1.0, beta=0.0)  D = alpha*q(A) @ q(B)^T + beta*C
+    fp4_linear(x, weight, bias=None)              F.linear with FP4 operands
+    FP4WeightCache(weight, bias=None)             quantize once, .forward(x, sync=True)
+    fp4_quantize(weight, bias=None)               -> FP4WeightCache
+    fp4_cached_matmul(A, cache), fp4_cached_linear(x, cache)
+    sync(), prealloc(max_M, max_N, max_K), cleanup(), SF_VEC_SIZE
+
+The work runs in ``libfp4gemm.so`` (beside this file, loaded through ctypes with
+tensors passed by pointer, as the reference does at fp4_gemm.py:26-27): a
+vectorised BF16->NVFP4 quantizer and a tcgen05 block-scaled GEMM.  Results
+equal the reference's: the reference zero-pads M, N, K to multiples of 128 and
+slices the output afterwards; here the kernels read the unpadded tensors
+(zeros outside, same quantized bytes) and write only the valid [M, N] block,
+so the pad and unpad copies disappear.  The bias is added inside the GEMM
+epilogue with the reference's rounding order (BF16 product, then a BF16 add).
+Work is issued on PyTorch's current CUDA stream; ``sync=True`` and
+``fp4_matmul`` synchronise the device exactly where the reference does.
+
+There is no fallback: importing this module fails if the library is missing.
+"""
+
+import ctypes
+import os
+
+import torch
+
+_lib_path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libfp4gemm.so")
+if not os.path.exists(_lib_path):
+    raise ImportError(
+        f"{_lib_path} is missing; build it with `python {os.path.join(os.path.dirname(_lib_path), 'build.py')}`")
+_lib = ctypes.CDLL(_lib_path)
+
+_vp, _i, _f = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+
+
+def _bind(name, restype, argtypes):
+    fn = getattr(_lib, name)
+    fn.restype = restype
+    fn.argtypes = argtypes
+    return fn
+
+
+# Reference ABI (fp4_gemm.py:30-84 of the reference binds the same signatures).
+_bind("fp4_gemm_sf_vec_size", _i, [])
+_bind("fp4_gemm_init", _i, [_i, _i, _i])
+_bind("fp4_gemm_run", _i, [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _f])
+_bind("fp4_gemm_cleanup", None, [])
+_bind("fp4_gemm_prealloc", _i, [_i, _i, _i])
+_bind("fp4_gemm_sync", None, [])
+_bind("fp4_quantize_weights", _vp, [_vp, _i, _i])
+_bind("fp4_weight_cache_free", None, [_vp])
+_bind("fp4_weight_cache_N", _i, [_vp])
+_bind("fp4_weight_cache_K", _i, [_vp])
+_bind("fp4_weight_cache_fp4_ptr", _vp, [_vp])
+_bind("fp4_weight_cache_sf_ptr", _vp, [_vp])
+_bind("fp4_gemm_run_cached", _i, [_vp, _vp, _vp, _vp, _i, _f, _f])
+# Additive ABI.
+_bind("fp4b_version", _i, [])
+_bind("fp4b_last_error", ctypes.c_char_p, [])
+_bind("fp4b_device_error", _i, [_i])
+_bind("fp4b_quantize", _i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp])
+_bind("fp4b_gemm_prequant", _i, [_vp, _vp, _i, _i, _vp, _vp, _i, _i, _i, _vp, _i, _vp, _i, _vp, _f, _f, _vp])
+_bind("fp4b_run_cached_ex", _i, [_vp, _i, _i, _i, _vp, _i, _vp, _i, _vp, _i, _vp, _f, _f, _vp])
+_bind("fp4b_run_ex", _i, [_vp, _i, _i, _i, _vp, _i, _i, _vp, _i, _vp, _i, _vp, _f, _f, _vp])
+_bind("fp4b_quantize_weights_ex", _vp, [_vp, _i, _i, _i, _vp, _i])
+_bind("fp4b_weight_cache_slice", _vp, [_vp, _i, _i])
+_bind("fp4b_weight_cache_export", _i, [_vp, _vp, _vp, _vp])
+_bind("fp4b_weight_cache_import", _vp, [_vp, _vp, _i, _i, _vp])
+
+# Query scale factor vector size
+SF_VEC_SIZE = _lib.fp4_gemm_sf_vec_size()
+
+
+def _pad_to_multiple(x: int, m: int) -> int:
+    """Round up x to the nearest multiple of m."""
+    return ((x + m - 1) // m) * m
+
+
+def _stream_ptr(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _last_error() -> str:
+    msg = _lib.fp4b_last_error()
+    return msg.decode() if msg else ""
+
+
+def _rows_view(t: torch.Tensor):
+    """(tensor, row stride) with unit column stride; copies only if needed."""
+    if t.dim() == 2 and t.stride(1) == 1 and t.stride(0) >= t.shape[1]:
+        return t, t.stride(0)
+    t = t.contiguous()
+    return t, t.shape[1]
+
+
+def fp4_matmul(
+    A: torch.Tensor,
+    B: torch.Tensor,
+    C: torch.Tensor = None,
+    alpha: float = 1.0,
+    beta: float = 0.0,
+) -> torch.Tensor:
+    """
+    FP4 matrix multiply on B200 tensor cores.
+
+    Computes: D = alpha * quantize_fp4(A) @ quantize_fp4(B)^T + beta * C
+
+    Args:
+        A: Input activation tensor [M, K] or [batch, M, K], BF16 on CUDA
+        B: Weight tensor [N, K], BF16 on CUDA
+        C: Optional bias/residual tensor [M, N], BF16 on CUDA
+        alpha: Scalar multiplier for GEMM result
+        beta: Scalar multiplier for C
+
+    Returns:
+        D: Output tensor [M, N] or [batch, M, N], BF16 on CUDA
+
+    Any M, N, K are accepted (the quantized operands are zero-padded to
+    multiples of 128 exactly as the reference pads them).  Synchronises the
+    device before returning, like the reference's fp4_gemm_run.
+    """
+    batched = A.dim() == 3
+    if batched:
+        batch_size = A.shape[0]
+        A = A.reshape(-1, A.shape[-1])
+
+    assert A.dim() == 2, f"A must be 2D [M, K] or 3D [batch, M, K], got shape {A.shape}"
+    assert B.dim() == 2, f"B must be 2D [N, K], got shape {B.shape}"
+    assert A.shape[1] == B.shape[1], f"K mismatch: A has K={A.shape[1]}, B has K={B.shape[1]}"
+    assert A.is_cuda and B.is_cuda, "Both tensors must be on CUDA"
+
+    M_orig, K_orig = A.shape
+    N_orig = B.shape[0]
+
+    if A.dtype != torch.bfloat16:
+        A = A.to(torch.bfloat16)
+    if B.dtype != torch.bfloat16:
+        B = B.to(torch.bfloat16)
+
+    D = torch.empty(M_orig, N_orig, dtype=torch.bfloat16, device=A.device)
+    if M_orig > 0 and N_orig > 0:
+        if K_orig == 0:
+            D.zero_()
+            if C is not None and beta != 0.0:
+                D = (beta * C.to(torch.bfloat16).float()).to(torch.bfloat16).reshape(M_orig, N_orig)
+        else:
+            A, lda = _rows_view(A)
+            B, ldb = _rows_view(B)
+            c_ptr, ldc = None, 0
+            if C is not None:
+                if C.dtype != torch.bfloat16:
+                    C = C.to(torch.bfloat16)
+                C = C.expand(M_orig, N_orig) if C.shape != (M_orig, N_orig) else C
+                C = C.contiguous()
+                c_ptr, ldc = C.data_ptr(), N_orig
+            with torch.cuda.device(A.device):
+                rc = _lib.fp4b_run_ex(A.data_ptr(), M_orig, K_orig, lda, B.data_ptr(), N_orig, ldb, c_ptr, ldc,
+                                      D.data_ptr(), N_orig, None, float(alpha), float(beta), _stream_ptr(A.device))
+                if rc != 0:
+                    raise RuntimeError(f"fp4_gemm_run failed with error code {rc} ({_last_error()})")
+                _lib.fp4_gemm_sync()
+
+    if batched:
+        D = D.reshape(batch_size, -1, N_orig)
+
+    return D
+
+
+def fp4_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor = None) -> torch.Tensor:
+    """
+    Drop-in replacement for F.linear using FP4 tensor cores.
+
+    Args:
+        x: Input tensor [..., K], BF16 on CUDA
+        weight: Weight tensor [N, K], BF16 on CUDA
+        bias: Optional bias [N], BF16 on CUDA
+
+    Returns:
+        Output tensor [..., N]
+    """
+    orig_shape = x.shape
+    x_2d = x.reshape(-1, x.shape[-1])
+
+    out = fp4_matmul(x_2d, weight)
+
+    if bias is not None:
+        out = out + bias.unsqueeze(0)
+
+    out = out.reshape(*orig_shape[:-1], weight.shape[0])
+    return out
+
+
+def sync():
+    """Synchronize the device. Call after pipelined FP4 operations."""
+    _lib.fp4_gemm_sync()
+
+
+def prealloc(max_M: int, max_N: int, max_K: int):
+    """
+    Pre-allocate internal buffers for the maximum expected dimensions.
+    Call once before inference to avoid reallocation during forward passes.
+
+    Args:
+        max_M: Maximum M dimension (batch_size * seq_len, rounded to 128)
+        max_N: Maximum N dimension across all weight matrices
+        max_K: Maximum K dimension across all weight matrices
+    """
+    max_M = _pad_to_multiple(max_M, 128)
+    max_N = _pad_to_multiple(max_N, 128)
+    max_K = _pad_to_multiple(max_K, 128)
+    rc = _lib.fp4_gemm_prealloc(max_M, max_N, max_K)
+    if rc != 0:
+        raise RuntimeError(f"fp4_gemm_prealloc failed with code {rc}")
+
+
+def cleanup():
+    """Release CUDA memory held by the FP4 GEMM library."""
+    _lib.fp4_gemm_cleanup()
+
+
+class FP4WeightCache:
+    """
+    Cached FP4 weights for fast inference.
+
+    Quantizes BF16 weights to NVFP4 format once, then reuses the
+    pre-quantized data for every GEMM call. Only activations get
+    quantized on the fly.
+
+    Usage:
+        cache = FP4WeightCache(weight)  # quantize once
+        output = cache.forward(x)       # fast inference
+        cache.free()                    # release GPU memory
+
+    Or as a context manager:
+        with FP4WeightCache(weight) as cache:
+            output = cache.forward(x)
+
+    The device bytes (``fp4_bytes`` packed E2M1 of the [N, K] weight padded to
+    multiples of 128, then ``sf_bytes`` scales) are identical to the
+    reference's cache for the same weight.
+    """
+
+    def __init__(self, weight: torch.Tensor, bias: torch.Tensor = None):
+        """
+        Quantize a weight matrix to FP4 and cache on device.
+
+        Args:
+            weight: [N, K] BF16 weight matrix on CUDA
+            bias: Optional [N] bias vector
+        """
+        self._handle = None
+        assert weight.dim() == 2, f"Weight must be 2D [N, K], got {weight.shape}"
+        assert weight.is_cuda, "Weight must be on CUDA"
+
+        self.N_orig = weight.shape[0]
+        self.K_orig = weight.shape[1]
+        self.bias = bias
+
+        # Padded (cached) shape, multiples of 128
+        self.N = _pad_to_multiple(self.N_orig, 128)
+        self.K = _pad_to_multiple(self.K_orig, 128)
+        self.padded = (self.N != self.N_orig or self.K != self.K_orig)
+
+        if weight.dtype != torch.bfloat16:
+            weight = weight.to(torch.bfloat16)
+        weight, ldw = _rows_view(weight)
+        self.device = weight.device
+
+        with torch.cuda.device(weight.device):
+            handle = _lib.fp4b_quantize_weights_ex(weight.data_ptr(), self.N_orig, self.K_orig, ldw,
+                                                   _stream_ptr(weight.device), 1)
+        if not handle:
+            raise RuntimeError("fp4_quantize_weights failed")
+        self._handle = handle
+
+        # Memory tracking
+        self.fp4_bytes = self.N * self.K // 2
+        # Scale factors: 1 byte per 16 elements
+        self.sf_bytes = self.N * (self.K // 16)
+
+    @classmethod
+    def _from_handle(cls, handle: int, n_orig: int, k_orig: int, device, bias=None):
+        obj = cls.__new__(cls)
+        obj._handle = handle
+        obj.N_orig, obj.K_orig, obj.bias = n_orig, k_orig, bias
+        obj.N = _lib.fp4_weight_cache_N(handle)
+        obj.K = _lib.fp4_weight_cache_K(handle)
+        obj.padded = (obj.N != n_orig or obj.K != k_orig)
+        obj.device = device
+        obj.fp4_bytes = obj.N * obj.K // 2
+        obj.sf_bytes = obj.N * (obj.K // 16)
+        return obj
+
+    def forward(self, x: torch.Tensor, sync: bool = True) -> torch.Tensor:
+        """
+        Run FP4 GEMM: output = x @ cached_weight.T + bias
+
+        Args:
+            x: Input activation [..., K], BF16 on CUDA
+            sync: If True, synchronize after GEMM. Set False for pipelined calls.
+
+        Returns:
+            Output tensor [..., N]
+        """
+        if self._handle is None:
+            raise RuntimeError("FP4WeightCache has been freed")
+
+        orig_shape = x.shape
+        x_2d = x.reshape(-1, x.shape[-1])
+
+        M_orig = x_2d.shape[0]
+        K_in = x_2d.shape[1]
+
+        if K_in != self.K_orig:
+            raise ValueError(f"Input K={K_in} doesn't match weight K={self.K_orig}")
+
+        if x_2d.dtype != torch.bfloat16:
+            x_2d = x_2d.to(torch.bfloat16)
+
+        bias = self.bias
+        fuse_bias = bias is not None and bias.dtype == torch.bfloat16 and bias.is_cuda
+        D = torch.empty(M_orig, self.N_orig, dtype=torch.bfloat16, device=x_2d.device)
+        if M_orig > 0:
+            x_2d, lda = _rows_view(x_2d)
+            b_ptr = None
+            if fuse_bias:
+                bias = bias.reshape(-1).contiguous()
+                b_ptr = bias.data_ptr()
+            with torch.cuda.device(x_2d.device):
+                rc = _lib.fp4b_run_cached_ex(x_2d.data_ptr(), M_orig, K_in, lda, self._handle, self.N_orig, None, 0,
+                                             D.data_ptr(), self.N_orig, b_ptr, 1.0, 0.0, _stream_ptr(x_2d.device))
+            if rc != 0:
+                raise RuntimeError(f"fp4_gemm_run_cached failed with error code {rc} ({_last_error()})")
+
+        # Sync if requested (skip for pipelined calls)
+        if sync:
+            _lib.fp4_gemm_sync()
+
+        if self.bias is not None and not fuse_bias:
+            D = D + self.bias.unsqueeze(0)
+
+        D = D.reshape(*orig_shape[:-1], self.N_orig)
+        return D
+
+    def shard(self, row0: int, rows: int, bias=None) -> "FP4WeightCache":
+        """A cache viewing rows [row0, row0+rows) of this one (multiples of 128), for N-sharding."""
+        h = _lib.fp4b_weight_cache_slice(self._handle, row0, rows)
+        if not h:
+            raise RuntimeError(f"fp4b_weight_cache_slice failed ({_last_error()})")
+        view = FP4WeightCache._from_handle(h, rows, self.K_orig, self.device, bias)
+        view._parent = self  # keep the owner alive
+        return view
+
+    def state_dict(self) -> dict:
+        """Serialisable payload: the cached bytes (device uint8 tensors) and shapes.
+
+        ``FP4WeightCache.from_state_dict`` rebuilds the cache without
+        re-quantizing (the reference re-quantizes at every model load)."""
+        if self._handle is None:
+            raise RuntimeError("FP4WeightCache has been freed")
+        fp4 = torch.empty(self.N, self.K // 2, dtype=torch.uint8, device=self.device)
+        sf = torch.empty(self.N * self.K // 16, dtype=torch.uint8, device=self.device)
+        with torch.cuda.device(self.device):
+            rc = _lib.fp4b_weight_cache_export(self._handle, fp4.data_ptr(), sf.data_ptr(), _stream_ptr(self.device))
+        if rc != 0:
+            raise RuntimeError(f"fp4b_weight_cache_export failed ({_last_error()})")
+        return {"fp4": fp4, "sf": sf, "N_orig": self.N_orig, "K_orig": self.K_orig, "bias": self.bias}
+
+    @classmethod
+    def from_state_dict(cls, sd: dict, device=None) -> "FP4WeightCache":
+        """Rebuild a cache from ``state_dict()`` output (tensors may be on the CPU)."""
+        device = torch.device(device) if device is not None else (
+            sd["fp4"].device if sd["fp4"].is_cuda else torch.device("cuda", torch.cuda.current_device()))
+        fp4 = sd["fp4"].to(device=device, dtype=torch.uint8).contiguous()
+        sf = sd["sf"].to(device=device, dtype=torch.uint8).contiguous()
+        n, k = fp4.shape[0], fp4.shape[1] * 2
+        assert sf.numel() == n * k // 16, "scale buffer size does not match the packed data"
+        with torch.cuda.device(device):
+            h = _lib.fp4b_weight_cache_import(fp4.data_ptr(), sf.data_ptr(), n, k, _stream_ptr(device))
+        if not h:
+            raise RuntimeError(f"fp4b_weight_cache_import failed ({_last_error()})")
+        return cls._from_handle(h, sd["N_orig"], sd["K_orig"], device, sd.get("bias"))
+
+    def free(self):
+        """Release GPU memory for cached weights."""
+        if getattr(self, "_handle", None):
+            _lib.fp4_weight_cache_free(ctypes.c_void_p(self._handle))
+            self._handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *args):
+        self.free()
+
+    def __del__(self):
+        self.free()
+
+    def __repr__(self):
+        status = "active" if self._handle else "freed"
+        mb = (self.fp4_bytes + self.sf_bytes) / (1024 * 1024)
+        return f"FP4WeightCache([{self.N_orig}, {self.K_orig}], {mb:.1f} MB, {status})"
+
+
+def fp4_quantize(weight: torch.Tensor, bias: torch.Tensor = None) -> FP4WeightCache:
+    """
+    Quantize a weight matrix to FP4 and cache on device.
+
+    Args:
+        weight: [N, K] BF16 weight matrix on CUDA
+        bias: Optional [N] bias vector
+
+    Returns:
+        FP4WeightCache handle for fast inference
+    """
+    return FP4WeightCache(weight, bias)
+
+
+def fp4_cached_matmul(
+    A: torch.Tensor,
+    cache: FP4WeightCache,
+) -> torch.Tensor:
+    """
+    FP4 matrix multiply with pre-quantized weights.
+
+    Computes: D = quantize_fp4(A) @ cached_B_fp4.T
+
+    Only A is quantized on the fly. B uses pre-quantized cache.
+
+    Args:
+        A: Input tensor [M, K] or [batch, M, K], BF16 on CUDA
+        cache: Pre-quantized weight cache from fp4_quantize()
+
+    Returns:
+        D: Output tensor [M, N] or [batch, M, N], BF16 on CUDA
+    """
+    return cache.forward(A)
+
+
+def fp4_cached_linear(
+    x: torch.Tensor,
+    cache: FP4WeightCache,
+) -> torch.Tensor:
+    """
+    Drop-in replacement for F.linear using cached FP4 weights.
+
+    Args:
+        x: Input tensor [..., K], BF16 on CUDA
+        cache: Pre-quantized weight cache (includes bias if provided)
+
+    Returns:
+        Output tensor [..., N]
+    """
+    return cache.forward(x)
+
+
+# ----------------------------------------------------------------------------
+# Lower-level helpers (additive; used by tests, benchmarks and fp4_gemm_dist)
+# ----------------------------------------------------------------------------
+
+def quantize_to_buffers(x: torch.Tensor, rows_pad: int = None, k_pad: int = None):
+    """Quantize a 2-D BF16 CUDA tensor into new (fp4 [rows_pad, k_pad/2], sf) uint8 tensors (async)."""
+    assert x.dim() == 2 and x.is_cuda and x.dtype == torch.bfloat16
+    rows, cols = x.shape
+    rows_pad = rows_pad or _pad_to_multiple(max(rows, 1), 128)
+    k_pad = k_pad or _pad_to_multiple(max(cols, 1), 128)
+    x, ld = _rows_view(x)
+    fp4 = torch.empty(rows_pad, k_pad // 2, dtype=torch.uint8, device=x.device)
+    sf = torch.empty(rows_pad * k_pad // 16, dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        rc = _lib.fp4b_quantize(x.data_ptr(), rows, cols, ld, fp4.data_ptr(), sf.data_ptr(), rows_pad, k_pad,
+                                _stream_ptr(x.device))
+    if rc != 0:
+        raise RuntimeError(f"fp4b_quantize failed with error code {rc} ({_last_error()})")
+    return fp4, sf
+
+
+def gemm_prequantized(a_fp4, a_sf, m: int, b_fp4, b_sf, n: int, k_pad: int, bias=None, C=None,
+                      alpha: float = 1.0, beta: float = 0.0, out=None):
+    """D[m, n] from already-quantized operands (async; BF16 out)."""
+    dev = a_fp4.device
+    D = out if out is not None else torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    c_ptr, ldc = (C.data_ptr(), C.stride(0)) if C is not None else (None, 0)
+    b_ptr = bias.data_ptr() if bias is not None else None
+    with torch.cuda.device(dev):
+        rc = _lib.fp4b_gemm_prequant(a_fp4.data_ptr(), a_sf.data_ptr(), m, a_fp4.shape[0], b_fp4.data_ptr(),
+                                     b_sf.data_ptr(), n, b_fp4.shape[0], k_pad, c_ptr, ldc, D.data_ptr(),
+                                     D.stride(0), b_ptr, float(alpha), float(beta), _stream_ptr(dev))
+    if rc != 0:
+        raise RuntimeError(f"fp4b_gemm_prequant failed with error code {rc} ({_last_error()})")
+    return D
+
+
+def device_error(clear: bool = True) -> int:
+    """Non-zero if a kernel gave up on a bounded wait (synchronises the device)."""
+    return _lib.fp4b_device_error(1 if clear else 0)

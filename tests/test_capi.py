@@ -1,0 +1,86 @@
+"""The C ABI library loads, exports every declared symbol, and rejects bad
+arguments on the host (no GPU work is issued by these tests)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from tests.conftest import PKG, ROOT
+
+HEADER = os.path.join(ROOT, "include", "fp4gemm.h")
+LIB = os.path.join(PKG, "libfp4gemm.so")
+
+# The symbols the reference library exports (fp4_gemm_lib.cu:401-842).
+REFERENCE_SYMBOLS = [
+    "fp4_gemm_sf_vec_size", "fp4_gemm_init", "fp4_gemm_prealloc", "fp4_gemm_run", "fp4_gemm_run_host",
+    "fp4_gemm_cleanup", "fp4_gemm_sync", "fp4_quantize_weights", "fp4_weight_cache_fp4_ptr",
+    "fp4_weight_cache_sf_ptr", "fp4_weight_cache_N", "fp4_weight_cache_K", "fp4_weight_cache_free",
+    "fp4_gemm_run_cached",
+]
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return re.findall(r"\b(fp4[A-Za-z0-9_]*)\s*\(", text)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    assert os.path.exists(LIB), "libfp4gemm.so not built"
+    return ctypes.CDLL(LIB)
+
+
+def test_header_declares_reference_abi():
+    decl = declared_functions()
+    assert set(REFERENCE_SYMBOLS) <= set(decl)
+
+
+def test_every_declared_symbol_is_exported(lib):
+    missing = [name for name in declared_functions() if not hasattr(lib, name)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_host_side_contract(lib):
+    lib.fp4_quantize_weights.restype = ctypes.c_void_p
+    lib.fp4b_weight_cache_slice.restype = ctypes.c_void_p
+    lib.fp4_weight_cache_fp4_ptr.restype = ctypes.c_void_p
+    lib.fp4b_last_error.restype = ctypes.c_char_p
+    assert lib.fp4_gemm_sf_vec_size() == 16
+    assert lib.fp4b_version() == 1
+    # shape errors are reported before any device work (fp4_gemm_lib.cu:673-676, 762-774)
+    assert lib.fp4_quantize_weights(None, 100, 128) is None
+    assert b"multiples of 128" in lib.fp4b_last_error()
+    assert lib.fp4_gemm_run_cached(None, None, None, None, 128, ctypes.c_float(1.0), ctypes.c_float(0.0)) == -1
+    assert lib.fp4_gemm_init(100, 128, 128) == -1
+    assert lib.fp4_gemm_run_host(None, None, None, None, 128, 128, 128, ctypes.c_float(1.0), ctypes.c_float(0.0)) == -2
+    # NULL handles: getters return 0 / NULL, free is NULL-safe (fp4_gemm_lib.cu:723-750)
+    assert lib.fp4_weight_cache_N(None) == 0 and lib.fp4_weight_cache_K(None) == 0
+    assert lib.fp4_weight_cache_fp4_ptr(None) is None
+    lib.fp4_weight_cache_free(None)
+    assert lib.fp4b_weight_cache_slice(None, 0, 128) is None
+
+
+def test_python_module_imports_without_gpu():
+    import fp4_gemm
+    assert fp4_gemm.SF_VEC_SIZE == 16
+    assert fp4_gemm._pad_to_multiple(2880, 128) == 2944
+    for name in ["fp4_matmul", "fp4_linear", "FP4WeightCache", "fp4_quantize", "fp4_cached_matmul",
+                 "fp4_cached_linear", "sync", "prealloc", "cleanup"]:
+        assert callable(getattr(fp4_gemm, name))
+
+
+def test_python_argument_errors_match_reference():
+    import torch
+
+    import fp4_gemm
+    w = torch.zeros(128, 128, dtype=torch.bfloat16)
+    with pytest.raises(AssertionError, match="Weight must be on CUDA"):
+        fp4_gemm.FP4WeightCache(w)
+    with pytest.raises(AssertionError, match="Weight must be 2D"):
+        fp4_gemm.FP4WeightCache(torch.zeros(4, dtype=torch.bfloat16))
+    with pytest.raises(AssertionError, match="K mismatch"):
+        fp4_gemm.fp4_matmul(torch.zeros(4, 8), torch.zeros(4, 16))
+    with pytest.raises(AssertionError, match="Both tensors must be on CUDA"):
+        fp4_gemm.fp4_matmul(torch.zeros(4, 8), torch.zeros(4, 8))

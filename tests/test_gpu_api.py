@@ -1,0 +1,184 @@
+"""The drop-in fp4_gemm API and the reference ABI on the GPU.
+
+Mirrors how the reference's Python layer (fp4_gemm.py:95-467) and C ABI
+(fp4_gemm_lib.cu:401-842) are used: weight caches whose bytes must equal the
+reference quantizer's, cached and dynamic linears within the GEMM tolerance,
+the padding rules, the sync behaviour and the error behaviour.
+"""
+import ctypes
+import hashlib
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from tests import workloads as W
+from tests.gpu_helpers import assert_gemm_close, oracle_linear, oracle_quantize
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def cache_bytes(fp4mod, cache):
+    sd = cache.state_dict()
+    torch.cuda.synchronize()
+    return sd["fp4"].cpu().numpy(), sd["sf"].cpu().numpy()
+
+
+@pytest.mark.parametrize("n,k", [(2880, 2880), (2880, 7680)])
+def test_weight_cache_bytes_equal_reference_digest(cuda, fp4, n, k):
+    key = f"cfg{1 if k == 2880 else 2}_weight_{n}x{k}_seed1"
+    want = json.load(open(os.path.join(GOLDEN, "digests.json")))[key]
+    w = W.normal_bf16((n, k), 0.02, 1).to(cuda)
+    with fp4.FP4WeightCache(w) as cache:
+        assert (cache.N, cache.K) == (2944, fp4._pad_to_multiple(k, 128))
+        q, s = cache_bytes(fp4, cache)
+    assert hashlib.sha256(q.tobytes()).hexdigest() == want["fp4"]
+    assert hashlib.sha256(s.tobytes()).hexdigest() == want["sf"]
+
+
+def test_reference_abi_quantize_weights_matches_padded_cache(cuda, fp4):
+    # fp4_quantize_weights on a zero-padded weight == the padding-free cache.
+    w = W.normal_bf16((200, 300), 0.02, 3)
+    wp = torch.zeros(256, 384, dtype=torch.bfloat16)
+    wp[:200, :300] = w
+    wp = wp.to(cuda)
+    h = fp4._lib.fp4_quantize_weights(wp.data_ptr(), 256, 384)
+    assert h
+    assert fp4._lib.fp4_weight_cache_N(h) == 256 and fp4._lib.fp4_weight_cache_K(h) == 384
+    ref = fp4.FP4WeightCache._from_handle(h, 256, 384, cuda)
+    q1, s1 = cache_bytes(fp4, ref)
+    with fp4.FP4WeightCache(w.to(cuda)) as c2:
+        q2, s2 = cache_bytes(fp4, c2)
+    rq, rs = oracle_quantize(w, 256, 384)
+    assert np.array_equal(q1, rq) and np.array_equal(s1, rs)
+    assert np.array_equal(q2, rq) and np.array_equal(s2, rs)
+    ref.free()
+    assert not fp4._lib.fp4_quantize_weights(wp.data_ptr(), 200, 384)  # N % 128 != 0 -> NULL
+
+
+@pytest.mark.parametrize("m,n,k,with_bias", [(256, 2880, 2880, False), (2048, 2880, 7680, True), (100, 300, 200, True),
+                                             (1, 64, 48, True)])
+def test_cached_linear_matches_oracle(cuda, fp4, m, n, k, with_bias):
+    x, w, b = W.cached_linear_inputs(m, n, k, seed=m + n + k, bias=with_bias)
+    cache = fp4.fp4_quantize(w.to(cuda), None if b is None else b.to(cuda))
+    out = fp4.fp4_cached_linear(x.to(cuda), cache)
+    assert out.shape == (m, n) and out.dtype == torch.bfloat16
+    assert_gemm_close(out, oracle_linear(x, w, bias=b), f"cached {m}x{n}x{k}")
+    cache.free()
+
+
+def test_cached_forward_shapes_sync_and_errors(cuda, fp4):
+    x, w, b = W.cached_linear_inputs(3 * 50, 256, 320, seed=9)
+    cache = fp4.FP4WeightCache(w.to(cuda), b.to(cuda))
+    x3 = x.reshape(3, 50, 320).to(cuda)
+    y = cache.forward(x3, sync=False)
+    torch.cuda.synchronize()
+    assert y.shape == (3, 50, 256)
+    assert_gemm_close(y.reshape(150, 256), oracle_linear(x, w, bias=b), "3-D input")
+    assert torch.equal(fp4.fp4_cached_matmul(x.to(cuda), cache), y.reshape(150, 256))
+    with pytest.raises(ValueError, match="doesn't match weight K"):
+        cache.forward(torch.zeros(4, 321, dtype=torch.bfloat16, device=cuda))
+    assert "FP4WeightCache([256, 320]" in repr(cache)
+    cache.free()
+    with pytest.raises(RuntimeError, match="has been freed"):
+        cache.forward(x3)
+    assert "freed" in repr(cache)
+
+
+def test_fp32_bias_promotes_like_reference(cuda, fp4):
+    x, w, _ = W.cached_linear_inputs(128, 128, 128, seed=4, bias=False)
+    b32 = torch.randn(128)
+    with fp4.FP4WeightCache(w.to(cuda), b32.to(cuda)) as cache:
+        y = cache.forward(x.to(cuda))
+    assert y.dtype == torch.float32  # bf16 + fp32 -> fp32, as in fp4_gemm.py:389-390
+    ref = oracle_linear(x, w).to(torch.bfloat16).float() + b32
+    assert_gemm_close(y, ref, "fp32 bias")
+
+
+def test_state_dict_roundtrip(cuda, fp4):
+    x, w, b = W.cached_linear_inputs(128, 384, 256, seed=12)
+    c1 = fp4.FP4WeightCache(w.to(cuda), b.to(cuda))
+    sd = c1.state_dict()
+    sd_cpu = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in sd.items()}
+    c2 = fp4.FP4WeightCache.from_state_dict(sd_cpu, device=cuda)
+    xd = x.to(cuda)
+    assert torch.equal(c1.forward(xd), c2.forward(xd))
+    c1.free()
+    c2.free()
+
+
+def test_shard_view_matches_full_cache(cuda, fp4):
+    x, w, _ = W.cached_linear_inputs(256, 512, 384, seed=13, bias=False)
+    full = fp4.FP4WeightCache(w.to(cuda))
+    xd = x.to(cuda)
+    y = full.forward(xd)
+    parts = [full.shard(r0, 128).forward(xd) for r0 in range(0, 512, 128)]
+    assert torch.equal(torch.cat(parts, dim=1), y)
+    full.free()
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 384, 512), (100, 200, 300), (8192, 8192, 8192)])
+def test_dynamic_matmul_matches_oracle(cuda, fp4, m, n, k):
+    g = torch.Generator().manual_seed(m + n)
+    a = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    b = torch.randn(n, k, generator=g).to(torch.bfloat16)
+    d = fp4.fp4_matmul(a.to(cuda), b.to(cuda))
+    if m * n * k > 2 ** 32:
+        # full-size config 3: compare a row/column sample against the oracle
+        rows = torch.arange(0, m, 97)
+        ref = oracle_linear(a[rows], b)
+        assert_gemm_close(d[rows], ref, "8192^3 sampled rows")
+    else:
+        assert_gemm_close(d, oracle_linear(a, b), f"dynamic {m}x{n}x{k}")
+
+
+def test_dynamic_c_alpha_beta_batched_and_linear(cuda, fp4):
+    g = torch.Generator().manual_seed(21)
+    a = torch.randn(2, 64, 256, generator=g).to(torch.bfloat16)
+    b = torch.randn(128, 256, generator=g).to(torch.bfloat16)
+    c = torch.randn(128, 128, generator=g).to(torch.bfloat16)
+    d = fp4.fp4_matmul(a.to(cuda), b.to(cuda), C=c.to(cuda), alpha=0.5, beta=2.0)
+    assert d.shape == (2, 64, 128)
+    assert_gemm_close(d.reshape(128, 128), oracle_linear(a.reshape(128, 256), b, alpha=0.5, beta=2.0, c=c), "C")
+    bias = torch.randn(128, generator=g).to(torch.bfloat16)
+    y = fp4.fp4_linear(a.to(cuda), b.to(cuda), bias.to(cuda))
+    assert y.shape == (2, 64, 128)
+    assert_gemm_close(y.reshape(128, 128), oracle_linear(a.reshape(128, 256), b, bias=bias), "fp4_linear")
+
+
+def test_reference_abi_run_and_run_cached(cuda, fp4):
+    lib = fp4._lib
+    m, n, k = 256, 384, 512
+    g = torch.Generator().manual_seed(31)
+    a = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    b = torch.randn(n, k, generator=g).to(torch.bfloat16)
+    c = torch.randn(m, n, generator=g).to(torch.bfloat16)
+    ad, bd, cd = a.to(cuda), b.to(cuda), c.to(cuda)
+    d = torch.zeros(m, n, dtype=torch.bfloat16, device=cuda)
+    assert lib.fp4_gemm_prealloc(512, 512, 512) == 0
+    assert lib.fp4_gemm_run(ad.data_ptr(), bd.data_ptr(), cd.data_ptr(), d.data_ptr(), m, n, k, 1.0, 0.5) == 0
+    assert_gemm_close(d, oracle_linear(a, b, beta=0.5, c=c), "fp4_gemm_run")
+    assert lib.fp4_gemm_run(ad.data_ptr(), bd.data_ptr(), None, d.data_ptr(), m, n, 200, 1.0, 0.0) != 0
+    h = lib.fp4_quantize_weights(bd.data_ptr(), n, k)
+    d2 = torch.zeros(m, n, dtype=torch.bfloat16, device=cuda)
+    assert lib.fp4_gemm_run_cached(ad.data_ptr(), h, None, d2.data_ptr(), m, 1.0, 0.0) == 0
+    lib.fp4_gemm_sync()
+    assert_gemm_close(d2, oracle_linear(a, b), "fp4_gemm_run_cached")
+    assert lib.fp4_gemm_run_cached(ad.data_ptr(), h, None, d2.data_ptr(), 100, 1.0, 0.0) == -1
+    assert lib.fp4_gemm_run_cached(ad.data_ptr(), None, None, d2.data_ptr(), m, 1.0, 0.0) == -1
+    lib.fp4_weight_cache_free(h)
+    fp4.cleanup()
+    assert fp4.device_error() == 0
+
+
+def test_prealloc_and_cleanup(cuda, fp4):
+    fp4.prealloc(4096, 7680, 5760)
+    fp4.cleanup()
+    with pytest.raises(RuntimeError):
+        # fp4_gemm_prealloc -> fp4_gemm_init returns -1 only when shapes are invalid
+        fp4._lib.fp4_gemm_cleanup()
+        if fp4._lib.fp4_gemm_prealloc(0, 0, 0) != 0:
+            raise RuntimeError("prealloc of an empty shape fails, as in the reference")

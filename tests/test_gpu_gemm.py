@@ -1,0 +1,99 @@
+"""tcgen05 block-scaled GEMM vs the fp32 matmul of the oracle-dequantized operands.
+
+The reference GEMM (CUTLASS SM120, fp4_gemm_lib.cu:540-580) is pinned only by
+this tolerance: D must match alpha * dq(A) @ dq(B)^T + beta*C (+ bias) in fp32
+within max rel-err 1e-2 (tests/gpu_helpers.py).  Every tile width the kernel
+has is forced in turn; ragged M/N/K, K tails of half a stage, C/alpha/beta and
+bias are covered, and the headline shape runs at full size.
+"""
+import numpy as np
+import pytest
+import torch
+
+from tests import workloads as W
+from tests.gpu_helpers import assert_gemm_close, oracle_dequant, oracle_linear, oracle_quantize, pearson
+
+pytestmark = pytest.mark.gpu
+
+TILES = [128, 160, 192, 224, 256]
+
+
+def run_prequant(fp4mod, x, w, bias=None, C=None, alpha=1.0, beta=0.0):
+    dev = torch.device("cuda:0")
+    m, k = x.shape
+    n = w.shape[0]
+    kp = fp4mod._pad_to_multiple(k, 128)
+    aq, asf = fp4mod.quantize_to_buffers(x.to(dev), None, kp)
+    bq, bsf = fp4mod.quantize_to_buffers(w.to(dev), None, kp)
+    d = fp4mod.gemm_prequantized(aq, asf, m, bq, bsf, n, kp, bias=None if bias is None else bias.to(dev),
+                                 C=None if C is None else C.to(dev), alpha=alpha, beta=beta)
+    torch.cuda.synchronize()
+    return d
+
+
+@pytest.mark.parametrize("bn", TILES)
+@pytest.mark.parametrize("m,n,k", [(128, 256, 256), (256, 512, 1024), (200, 300, 384), (1, 8, 128),
+                                   (384, 1000, 640)])
+def test_tile_widths(cuda, fp4, monkeypatch, bn, m, n, k):
+    monkeypatch.setenv("FP4B_FORCE_BN", str(bn))
+    x = W.normal_bf16((m, k), 1.0, m + n)
+    w = W.normal_bf16((n, k), 1.0, k)
+    d = run_prequant(fp4, x, w)
+    assert_gemm_close(d, oracle_linear(x, w), f"bn={bn} {m}x{n}x{k}")
+    assert fp4.device_error() == 0
+
+
+def test_alpha_beta_c_bias(cuda, fp4):
+    m, n, k = 256, 384, 512
+    x = W.normal_bf16((m, k), 1.0, 1)
+    w = W.normal_bf16((n, k), 0.02, 2)
+    c = W.normal_bf16((m, n), 1.0, 3)
+    b = W.normal_bf16((n,), 0.01, 4)
+    for alpha, beta in ((1.0, 0.0), (0.5, 1.0), (2.0, -0.25)):
+        d = run_prequant(fp4, x, w, bias=b, C=c, alpha=alpha, beta=beta)
+        ref = oracle_linear(x, w, bias=b, alpha=alpha, beta=beta, c=c)
+        assert_gemm_close(d, ref, f"alpha={alpha} beta={beta}")
+
+
+def test_n_not_multiple_of_8(cuda, fp4):
+    x = W.normal_bf16((130, 256), 1.0, 5)
+    w = W.normal_bf16((37, 256), 1.0, 6)
+    d = run_prequant(fp4, x, w)
+    assert_gemm_close(d, oracle_linear(x, w), "n=37")
+
+
+def test_headline_shape_full_size(cuda, fp4):
+    m, n, k = W.HEADLINE_SHAPE
+    x, w, b = W.cached_linear_inputs(m, n, k, seed=0)
+    d = run_prequant(fp4, x, w, bias=b)
+    ref = oracle_linear(x, w, bias=b)
+    assert_gemm_close(d, ref, "2048x2880x7680")
+    # accuracy vs unquantized fp32 is a property of NVFP4 with the reference's
+    # scale rounding, not of the kernel: it must equal the oracle's own value.
+    exact = x.float() @ w.float().t() + b.float()
+    assert abs(pearson(d, exact) - pearson(ref, exact)) < 2e-4
+
+
+def test_accumulation_over_long_k(cuda, fp4):
+    # K = 16384 exercises many pipeline wraps of the smem ring.
+    x = W.normal_bf16((128, 16384), 1.0, 8)
+    w = W.normal_bf16((256, 16384), 1.0, 9)
+    d = run_prequant(fp4, x, w)
+    assert_gemm_close(d, oracle_linear(x, w), "K=16384")
+
+
+def test_exact_small_integers(cuda, fp4):
+    # Operands that quantize exactly (values in E2M1 x power-of-two scales):
+    # the product is exact in fp32, so the result must equal the oracle bit for bit.
+    g = torch.Generator().manual_seed(3)
+    vals = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
+    x = vals[torch.randint(0, 8, (128, 256), generator=g)] * torch.where(torch.rand(128, 256, generator=g) < .5, -1, 1)
+    w = vals[torch.randint(0, 8, (128, 256), generator=g)]
+    x[:, ::16] = 6.0
+    w[:, ::16] = 6.0
+    x, w = x.to(torch.bfloat16), w.to(torch.bfloat16)
+    d = run_prequant(fp4, x, w)
+    ref = (x.float() @ w.float().t())
+    assert torch.equal(d.float().cpu(), ref.to(torch.bfloat16).float())
+    aq, asf = oracle_quantize(x)
+    assert torch.equal(oracle_dequant(aq, asf, 128, 256), x.float())
