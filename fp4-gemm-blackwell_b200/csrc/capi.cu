@@ -40,8 +40,11 @@ struct DeviceState {
     Buffer a_fp4, a_sf, b_fp4, b_sf;
 };
 
+// g_mu guards the scratch state; launchers run while it is held, so anything
+// they call (device_error_word) must use its own lock.
 std::mutex g_mu;
 DeviceState g_state[kMaxDevices];
+std::mutex g_err_mu;
 int* g_err_word[kMaxDevices];
 
 struct WeightCache {
@@ -159,7 +162,7 @@ int gemm_into(const GemmArgs& g, cudaStream_t st) {
 
 int* device_error_word() {
     const int d = current_device();
-    std::lock_guard<std::mutex> lk(g_mu);
+    std::lock_guard<std::mutex> lk(g_err_mu);
     if (!g_err_word[d]) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) {

@@ -54,9 +54,13 @@ constexpr int max_row_tiles(int bn) {
     return best;
 }
 
+// Tile widths are multiples of 64, so every tile starts 0 or 64 rows into a
+// 128-row scale atom and the MMA's scale-B TMEM address moves by 0 or 2
+// columns.  An odd column (a tile starting 32 or 96 rows into an atom, e.g.
+// BN = 160) raised a misaligned-address error on B200.
 template <int BN, int STAGES>
 struct Cfg {
-    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
+    static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 64 in [64, 256]");
     static constexpr int NRT = max_row_tiles(BN);
     static constexpr int A_BYTES = kBM * kStageKBytes;
     static constexpr int B_BYTES = BN * kStageKBytes;
@@ -356,7 +360,7 @@ cudaError_t launch_tile(const GemmArgs& g, cudaStream_t stream, int sms) {
 
 // Pick the tile width that minimises (waves x BN) on this device.
 int choose_bn(long m, long n, int sms) {
-    static const int cands[] = {256, 224, 192, 160, 128};
+    static const int cands[] = {256, 192, 128};
     const long mt = (m + kBM - 1) / kBM;
     int best = 128;
     long best_cost = -1;
@@ -396,9 +400,7 @@ cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     const int bn = force ? atoi(force) : choose_bn(g.m, g.n_out, sms);
     switch (bn) {
         case 256: return launch_tile<256, 4>(g, stream, sms);
-        case 224: return launch_tile<224, 4>(g, stream, sms);
         case 192: return launch_tile<192, 4>(g, stream, sms);
-        case 160: return launch_tile<160, 5>(g, stream, sms);
         case 128: return launch_tile<128, 6>(g, stream, sms);
         default: return cudaErrorInvalidValue;
     }

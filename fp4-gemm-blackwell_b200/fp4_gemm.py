@@ -385,7 +385,10 @@ class FP4WeightCache:
             h = _lib.fp4b_weight_cache_import(fp4.data_ptr(), sf.data_ptr(), n, k, _stream_ptr(device))
         if not h:
             raise RuntimeError(f"fp4b_weight_cache_import failed ({_last_error()})")
-        return cls._from_handle(h, sd["N_orig"], sd["K_orig"], device, sd.get("bias"))
+        bias = sd.get("bias")
+        if bias is not None:
+            bias = bias.to(device)
+        return cls._from_handle(h, sd["N_orig"], sd["K_orig"], device, bias)
 
     def free(self):
         """Release GPU memory for cached weights."""

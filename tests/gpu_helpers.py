@@ -58,8 +58,8 @@ def to_numpy_u8(t: torch.Tensor) -> np.ndarray:
 
 
 def pearson(a: torch.Tensor, b: torch.Tensor) -> float:
-    a = a.double().flatten()
-    b = b.double().flatten()
+    a = a.detach().cpu().double().flatten()
+    b = b.detach().cpu().double().flatten()
     a = a - a.mean()
     b = b - b.mean()
     return float((a @ b) / (a.norm() * b.norm()))

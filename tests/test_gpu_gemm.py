@@ -15,7 +15,7 @@ from tests.gpu_helpers import assert_gemm_close, oracle_dequant, oracle_linear, 
 
 pytestmark = pytest.mark.gpu
 
-TILES = [128, 160, 192, 224, 256]
+TILES = [128, 192, 256]
 
 
 def run_prequant(fp4mod, x, w, bias=None, C=None, alpha=1.0, beta=0.0):
@@ -71,7 +71,7 @@ def test_headline_shape_full_size(cuda, fp4):
     # accuracy vs unquantized fp32 is a property of NVFP4 with the reference's
     # scale rounding, not of the kernel: it must equal the oracle's own value.
     exact = x.float() @ w.float().t() + b.float()
-    assert abs(pearson(d, exact) - pearson(ref, exact)) < 2e-4
+    assert abs(pearson(d.cpu(), exact) - pearson(ref, exact)) < 2e-4
 
 
 def test_accumulation_over_long_k(cuda, fp4):
