@@ -6,17 +6,26 @@
 // elements in the 128x4 interleaved layout (the layout tcgen05 wants, so the
 // scale bytes are copied to tensor memory as they are).
 //
-// One CTA computes a 128 x BN tile, 192 threads in three roles:
-//   warp 0     TMA producer: per 256-wide K stage, one 2-D TMA (128B swizzle)
-//              for the A tile and one for the B tile, plus 1-D bulk copies of
-//              the contiguous 512-byte scale atoms, all completing on the
-//              stage's `full` mbarrier;
-//   warp 1     allocates TMEM and, from one elected lane, issues tcgen05.cp of
-//              the scale atoms into TMEM and four
-//              tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (K = 64 each)
-//              per stage; tcgen05.commit frees the stage's smem;
-//   warps 2-5  epilogue: tcgen05.ld the fp32 accumulator (one row per
-//              thread), alpha/beta/C, BF16, optional bias, 16-byte stores.
+// Persistent kernel, one CTA per SM walking 128 x BN output tiles; 192
+// threads in three roles:
+//   warp 0     TMA producer.  A stage covers K = 512: two 128-byte-wide TMA
+//              boxes (128B swizzle) for A, two for B, one bulk copy of the A
+//              scale atoms and one per 128-row tile of B scales, all
+//              completing on the stage's `full` mbarrier.  A copy completes
+//              one at a time per issuing thread (~0.4 us each from L2), so the
+//              copies of a stage go out from different lanes, and consecutive
+//              stages use different lanes.
+//   warp 1     allocates TMEM and walks the same loop converged; one elected
+//              lane issues per stage the tcgen05.cp of the scale atoms and
+//              eight tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (K = 64
+//              each), then tcgen05.commit frees the stage.  Issuing from a
+//              converged warp with unrolled, predicated k-block loops keeps
+//              the tensor pipe fed; issuing from a lone diverged thread was
+//              several times slower on B200.
+//   warps 2-5  epilogue: tcgen05.ld the fp32 accumulator (one row per thread),
+//              alpha/beta/C, BF16, optional bias, 16-byte stores.  Two TMEM
+//              accumulators (when they fit) let the epilogue of one tile run
+//              under the MMAs of the next.
 // No TMA multicast anywhere (the library also runs on multi-GPU nodes).
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -34,16 +43,17 @@ namespace fp4b {
 namespace {
 
 constexpr int kBM = 128;            // rows of A per tile (one tcgen05 M)
-constexpr int kStageKBytes = 128;   // K bytes per stage and row (256 FP4 elements)
-constexpr int kKbPerStage = 4;      // 64-element MMA k-blocks per stage
+constexpr int kChunkBytes = 128;    // one 128B-swizzle atom row: 256 FP4 elements of K
+constexpr int kChunks = 2;          // chunks per stage: a stage covers K = 512
+constexpr int kStageKBytes = kChunks * kChunkBytes;
+constexpr int kKbPerStage = 8;      // 64-element MMA k-blocks per stage
 constexpr int kAtomBytes = 512;     // 128 rows x 4 scale bytes
 constexpr int kThreads = 192;
+constexpr int kEpilogueWarps = 4;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemSfaCol = 256;
-constexpr uint32_t kTmemSfbCol = kTmemSfaCol + 4 * kKbPerStage;
 
 // Largest number of 128-row scale tiles one BN-wide tile can touch when tiles
-// start at multiples of BN (all starts are multiples of 32).
+// start at multiples of BN (starts are multiples of 64, see Cfg).
 constexpr int max_row_tiles(int bn) {
     int best = 0;
     for (int t = 0; t < 128; ++t) {
@@ -62,16 +72,23 @@ template <int BN, int STAGES>
 struct Cfg {
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 64 in [64, 256]");
     static constexpr int NRT = max_row_tiles(BN);
-    static constexpr int A_BYTES = kBM * kStageKBytes;
-    static constexpr int B_BYTES = BN * kStageKBytes;
+    static constexpr int A_CHUNK = kBM * kChunkBytes;   // one TMA box
+    static constexpr int B_CHUNK = BN * kChunkBytes;
+    static constexpr int A_BYTES = kChunks * A_CHUNK;
+    static constexpr int B_BYTES = kChunks * B_CHUNK;
     static constexpr int SFA_BYTES = kKbPerStage * kAtomBytes;
     static constexpr int SFB_BYTES = NRT * kKbPerStage * kAtomBytes;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    // TMEM columns: ACC_BUFS accumulators of BN fp32 columns, then the scales
+    // of one stage (4 k-blocks x 4 columns for A, 4 x 4*NRT for B).
+    static constexpr int SF_COLS = 4 * kKbPerStage * (1 + NRT);
+    static constexpr int ACC_BUFS = (2 * BN + SF_COLS <= (int)kTmemCols) ? 2 : 1;
+    static constexpr uint32_t TMEM_SFA = ACC_BUFS * BN;
+    static constexpr uint32_t TMEM_SFB = TMEM_SFA + 4 * kKbPerStage;
     static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
-    static_assert(kTmemSfbCol + kKbPerStage * 4 * NRT <= kTmemCols, "TMEM budget exceeded");
-    static_assert(BN <= (int)kTmemSfaCol, "accumulator overlaps the scale columns");
+    static_assert(TMEM_SFA + SF_COLS <= kTmemCols, "TMEM budget exceeded");
 };
 
 struct Params {
@@ -83,6 +100,7 @@ struct Params {
     int* err;
     int m, n_out, num_kb;  // num_kb = k_pad / 64
     int n_rows_pad;
+    int n_tiles, num_tiles;
     long ldc, ldd;
     float alpha, beta;
     int vec_store;  // D/C rows 16-byte aligned
@@ -102,6 +120,57 @@ __device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
+__device__ __forceinline__ bool aborted(const int* flag) { return *reinterpret_cast<const volatile int*>(flag) != 0; }
+
+// Epilogue of one 32-column chunk for one output row: alpha*acc (+beta*C),
+// BF16, (+bias in BF16), 16-byte stores.
+__device__ __forceinline__ void store_chunk(const Params& p, const uint32_t (&r)[32], int m, int nb) {
+    __nv_bfloat16* drow = p.d + (size_t)m * p.ldd;
+    const __nv_bfloat16* crow = p.c ? p.c + (size_t)m * p.ldc : nullptr;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        const int n = nb + 8 * g;
+        if (n >= p.n_out) break;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = p.alpha * __uint_as_float(r[8 * g + i]);
+        const bool full8 = p.vec_store && n + 8 <= p.n_out;
+        if (p.beta != 0.0f && crow) {
+            if (full8) {
+                const uint4 cv = *reinterpret_cast<const uint4*>(crow + n);
+                const __nv_bfloat16* cb = reinterpret_cast<const __nv_bfloat16*>(&cv);
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    v[i] = fmaf(p.alpha, __uint_as_float(r[8 * g + i]), p.beta * __bfloat162float(cb[i]));
+            } else {
+                for (int i = 0; i < 8 && n + i < p.n_out; ++i)
+                    v[i] = fmaf(p.alpha, __uint_as_float(r[8 * g + i]), p.beta * __bfloat162float(crow[n + i]));
+            }
+        }
+        if (p.bias) {
+            // Reference order: BF16 GEMM output, then a BF16 bias add.
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float b = (n + i < p.n_out) ? __bfloat162float(p.bias[n + i]) : 0.0f;
+                v[i] = __bfloat162float(__float2bfloat16_rn(v[i])) + b;
+            }
+        }
+        if (full8) {
+            uint4 o;
+            o.x = bf16x2_bits(v[0], v[1]);
+            o.y = bf16x2_bits(v[2], v[3]);
+            o.z = bf16x2_bits(v[4], v[5]);
+            o.w = bf16x2_bits(v[6], v[7]);
+            *reinterpret_cast<uint4*>(drow + n) = o;
+        } else {
+            for (int i = 0; i < 8 && n + i < p.n_out; ++i) drow[n + i] = __float2bfloat16_rn(v[i]);
+        }
+    }
+}
+
+// Persistent kernel: CTA b processes tiles b, b + gridDim.x, ... (N fastest).
+// The smem ring and the TMEM accumulators carry across tiles, so loads of the
+// next tile and the epilogue of the previous one overlap the MMAs.
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     nvf4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -115,15 +184,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* sSFB = sSFA + STAGES * C::SFA_BYTES;
     uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + STAGES * C::SFB_BYTES);
     uint64_t* empty = full + STAGES;
-    uint64_t* acc_full = empty + STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    uint64_t* acc_full = empty + STAGES;     // [2]
+    uint64_t* acc_empty = acc_full + 2;      // [2]
+    uint64_t* mma_done = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
     int* s_last_issued = s_abort + 1;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN;
-    const int m0 = blockIdx.y * kBM;
     const int num_kb = p.num_kb;
     const int num_ks = (num_kb + kKbPerStage - 1) / kKbPerStage;
 
@@ -132,7 +201,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mbar_init(&full[s], 1);
             ptx::mbar_init(&empty[s], 1);
         }
-        ptx::mbar_init(acc_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            ptx::mbar_init(&acc_full[b], 1);
+            ptx::mbar_init(&acc_empty[b], kEpilogueWarps);
+        }
+        ptx::mbar_init(mma_done, 1);
         *s_abort = 0;
         *s_last_issued = -1;
         ptx::fence_mbar_init();
@@ -148,140 +221,191 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // Scale row tiles covering B rows [n0, n0 + BN), clipped to the buffer.
-    const int rt0 = n0 >> 7;
-    const int shift_words = (n0 & 127) >> 5;
-    int nrt = ((n0 & 127) + BN + 127) >> 7;
-    if (rt0 + nrt > (p.n_rows_pad >> 7)) nrt = (p.n_rows_pad >> 7) - rt0;
-
     if (warp == 0) {
         // ------------------------------------------------------------ producer
-        if (ptx::elect_one()) {
-            const uint8_t* sfa_tile = p.a_sf + (size_t)blockIdx.y * kAtomBytes * num_kb;
-            for (int ks = 0; ks < num_ks; ++ks) {
-                const int s = ks % STAGES;
-                if (ks >= STAGES && !ptx::mbar_wait(&empty[s], ((ks / STAGES) & 1) ^ 1)) {
-                    record_error(p.err, kErrProducerTimeout);
-                    atomicExch(s_abort, 1);
+        // A TMA or bulk copy completes one at a time per issuing thread, so the
+        // loads of a stage are spread over up to 7 lanes, and consecutive stages
+        // use different groups of 8 lanes: 4 stages can be in flight at once.
+        int it = 0;
+        bool stop = false;
+        for (int t = blockIdx.x; t < p.num_tiles && !stop; t += gridDim.x) {
+            const int m_tile = t / p.n_tiles;
+            const int n0 = (t - m_tile * p.n_tiles) * BN;
+            const int m0 = m_tile * kBM;
+            const int rt0 = n0 >> 7;
+            int nrt = ((n0 & 127) + BN + 127) >> 7;
+            if (rt0 + nrt > (p.n_rows_pad >> 7)) nrt = (p.n_rows_pad >> 7) - rt0;
+            const uint8_t* sfa_tile = p.a_sf + (size_t)m_tile * kAtomBytes * num_kb;
+            for (int ks = 0; ks < num_ks; ++ks, ++it) {
+                const int s = it % STAGES;
+                if (it >= STAGES) {
+                    const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1));
+                    if (!ok) {
+                        if (lane == 0) {
+                            record_error(p.err, kErrProducerTimeout);
+                            atomicExch(s_abort, 1);
+                        }
+                        stop = true;
+                        break;
+                    }
+                }
+                if (__any_sync(0xffffffffu, aborted(s_abort))) {
+                    stop = true;
                     break;
                 }
-                if (*reinterpret_cast<volatile int*>(s_abort)) break;
                 const int kb0 = ks * kKbPerStage;
                 const int nkb = min(kKbPerStage, num_kb - kb0);
                 const uint32_t sf_bytes = (uint32_t)nkb * kAtomBytes;
-                ptx::mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES + sf_bytes * (1 + nrt));
-                ptx::tma_load_2d(sA + s * C::A_BYTES, &tmap_a, &full[s], ks * kStageKBytes, m0);
-                ptx::tma_load_2d(sB + s * C::B_BYTES, &tmap_b, &full[s], ks * kStageKBytes, n0);
-                ptx::bulk_load(sSFA + s * C::SFA_BYTES, sfa_tile + (size_t)kb0 * kAtomBytes, sf_bytes, &full[s]);
-                for (int j = 0; j < nrt; ++j) {
-                    const uint8_t* src = p.b_sf + ((size_t)(rt0 + j) * num_kb + kb0) * kAtomBytes;
-                    ptx::bulk_load(sSFB + s * C::SFB_BYTES + j * kKbPerStage * kAtomBytes, src, sf_bytes, &full[s]);
+                const int j = lane - (it & 3) * 8;
+                if (j == 0) ptx::mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES + sf_bytes * (1 + nrt));
+                __syncwarp();
+                const int kx = ks * kStageKBytes;
+                if (j == 0 || j == 1) {
+                    ptx::tma_load_2d(sA + s * C::A_BYTES + j * C::A_CHUNK, &tmap_a, &full[s], kx + j * kChunkBytes, m0);
+                } else if (j == 2 || j == 3) {
+                    ptx::tma_load_2d(sB + s * C::B_BYTES + (j - 2) * C::B_CHUNK, &tmap_b, &full[s],
+                                     kx + (j - 2) * kChunkBytes, n0);
+                } else if (j == 4) {
+                    ptx::bulk_load(sSFA + s * C::SFA_BYTES, sfa_tile + (size_t)kb0 * kAtomBytes, sf_bytes, &full[s]);
+                } else if (j >= 5 && j < 5 + nrt) {
+                    const int rt = j - 5;
+                    const uint8_t* src = p.b_sf + ((size_t)(rt0 + rt) * num_kb + kb0) * kAtomBytes;
+                    ptx::bulk_load(sSFB + s * C::SFB_BYTES + rt * kKbPerStage * kAtomBytes, src, sf_bytes, &full[s]);
                 }
-                *s_last_issued = ks;
+                __syncwarp();
+                if (lane == 0) *s_last_issued = it;
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        if (ptx::elect_one()) {
-            constexpr uint32_t idesc = ptx::idesc_nvf4(BN);
-            const uint32_t a_base = ptx::smem_u32(sA), b_base = ptx::smem_u32(sB);
-            const uint32_t sfa_base = ptx::smem_u32(sSFA), sfb_base = ptx::smem_u32(sSFB);
-            for (int ks = 0; ks < num_ks; ++ks) {
-                const int s = ks % STAGES;
-                if (!ptx::mbar_wait(&full[s], (ks / STAGES) & 1)) {
-                    record_error(p.err, kErrMmaTimeout);
-                    atomicExch(s_abort, 1);
+        // The whole warp walks the loop (so stage indices and descriptors are
+        // warp-uniform values) and one elected lane issues each stage's
+        // tcgen05 instructions from fully unrolled, predicated k-block loops.
+        const uint64_t adesc0 = ptx::desc_kmajor_sw128(ptx::smem_u32(sA));
+        const uint64_t bdesc0 = ptx::desc_kmajor_sw128(ptx::smem_u32(sB));
+        const uint64_t sfadesc0 = ptx::desc_sf_atom(ptx::smem_u32(sSFA));
+        const uint64_t sfbdesc0 = ptx::desc_sf_atom(ptx::smem_u32(sSFB));
+        constexpr uint32_t idesc = ptx::idesc_nvf4(BN);
+        int it = 0, tile_iter = 0;
+        bool stop = false;
+        for (int t = blockIdx.x; t < p.num_tiles && !stop; t += gridDim.x, ++tile_iter) {
+            const int n0 = (t % p.n_tiles) * BN;
+            int nrt = ((n0 & 127) + BN + 127) >> 7;
+            if ((n0 >> 7) + nrt > (p.n_rows_pad >> 7)) nrt = (p.n_rows_pad >> 7) - (n0 >> 7);
+            const uint32_t shift_words = (n0 & 127) >> 5;
+            const int b = tile_iter % C::ACC_BUFS;
+            if (tile_iter >= C::ACC_BUFS) {
+                const bool ok =
+                    __all_sync(0xffffffffu, ptx::mbar_wait(&acc_empty[b], ((tile_iter / C::ACC_BUFS) & 1) ^ 1));
+                if (!ok) {
+                    if (lane == 0) {
+                        record_error(p.err, kErrMmaTimeout);
+                        atomicExch(s_abort, 1);
+                    }
+                    break;
+                }
+            }
+            ptx::tc_fence_after();
+            const uint32_t acc = tmem + b * BN;
+            const uint32_t sfa_t = tmem + C::TMEM_SFA;
+            const uint32_t sfb_t = tmem + C::TMEM_SFB;
+            for (int ks = 0; ks < num_ks; ++ks, ++it) {
+                const int s = it % STAGES;
+                const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(&full[s], (it / STAGES) & 1));
+                if (!ok || __any_sync(0xffffffffu, aborted(s_abort))) {
+                    if (lane == 0) {
+                        record_error(p.err, kErrMmaTimeout);
+                        atomicExch(s_abort, 1);
+                    }
+                    stop = true;
                     break;
                 }
                 ptx::tc_fence_after();
                 const int nkb = min(kKbPerStage, num_kb - ks * kKbPerStage);
-                for (int j = 0; j < nkb; ++j) {
-                    ptx::tc_cp_32x128b_warpx4(tmem + kTmemSfaCol + 4 * j,
-                                              ptx::desc_sf_atom(sfa_base + s * C::SFA_BYTES + j * kAtomBytes));
-                    for (int t = 0; t < nrt; ++t)
-                        ptx::tc_cp_32x128b_warpx4(
-                            tmem + kTmemSfbCol + j * 4 * C::NRT + 4 * t,
-                            ptx::desc_sf_atom(sfb_base + s * C::SFB_BYTES + (t * kKbPerStage + j) * kAtomBytes));
+                // Descriptor start addresses are in 16-byte units in the low bits.
+                const uint64_t a_s = adesc0 + (uint64_t)((s * C::A_BYTES) >> 4);
+                const uint64_t b_s = bdesc0 + (uint64_t)((s * C::B_BYTES) >> 4);
+                const uint64_t sfa_s = sfadesc0 + (uint64_t)((s * C::SFA_BYTES) >> 4);
+                const uint64_t sfb_s = sfbdesc0 + (uint64_t)((s * C::SFB_BYTES) >> 4);
+                const uint32_t first = (ks == 0) ? 0u : 1u;
+                if (ptx::elect_one()) {
+#pragma unroll
+                    for (int j = 0; j < kKbPerStage; ++j) {
+                        if (j < nkb) {
+                            ptx::tc_cp_32x128b_warpx4(sfa_t + 4 * j, sfa_s + (uint64_t)((j * kAtomBytes) >> 4));
+#pragma unroll
+                            for (int r = 0; r < C::NRT; ++r)
+                                if (r < nrt)
+                                    ptx::tc_cp_32x128b_warpx4(
+                                        sfb_t + j * 4 * C::NRT + 4 * r,
+                                        sfb_s + (uint64_t)(((r * kKbPerStage + j) * kAtomBytes) >> 4));
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < kKbPerStage; ++j) {
+                        if (j < nkb) {
+                            const uint32_t koff = (uint32_t)(((j >> 2) * C::A_CHUNK + 32 * (j & 3)) >> 4);
+                            const uint32_t kofb = (uint32_t)(((j >> 2) * C::B_CHUNK + 32 * (j & 3)) >> 4);
+                            ptx::tc_mma_nvf4(acc, a_s + koff, b_s + kofb, idesc, sfa_t + 4 * j,
+                                             sfb_t + j * 4 * C::NRT + shift_words, (j == 0) ? first : 1u);
+                        }
+                    }
+                    ptx::tc_commit(&empty[s]);
                 }
-                for (int j = 0; j < nkb; ++j) {
-                    const uint64_t adesc = ptx::desc_kmajor_sw128(a_base + s * C::A_BYTES + 32 * j);
-                    const uint64_t bdesc = ptx::desc_kmajor_sw128(b_base + s * C::B_BYTES + 32 * j);
-                    ptx::tc_mma_nvf4(tmem, adesc, bdesc, idesc, tmem + kTmemSfaCol + 4 * j,
-                                     tmem + kTmemSfbCol + j * 4 * C::NRT + shift_words, (ks | j) != 0);
-                }
-                ptx::tc_commit(&empty[s]);
+                __syncwarp();
             }
-            ptx::tc_commit(acc_full);  // also on abort: completes once issued MMAs are done
+            if (!stop) {
+                if (ptx::elect_one()) ptx::tc_commit(&acc_full[b]);
+                __syncwarp();
+            }
         }
+        if (ptx::elect_one()) ptx::tc_commit(mma_done);  // completes once every MMA issued above is done
+        __syncwarp();
     } else {
         // ------------------------------------------------------------ epilogue
         const int q = warp & 3;  // TMEM lane quadrant this warp may read
-        const int row = q * 32 + lane;
-        const int m = m0 + row;
-        const bool ok = ptx::mbar_wait(acc_full, 0);
-        if (!ok) record_error(p.err, kErrEpilogueTimeout);
-        ptx::tc_fence_after();
-        const bool aborted = !ok || *reinterpret_cast<volatile int*>(s_abort);
-        if (!aborted) {
+        int tile_iter = 0;
+        for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++tile_iter) {
+            const int m_tile = t / p.n_tiles;
+            const int n0 = (t - m_tile * p.n_tiles) * BN;
+            const int m = m_tile * kBM + q * 32 + lane;
+            const int b = tile_iter % C::ACC_BUFS;
+            const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(&acc_full[b], (tile_iter / C::ACC_BUFS) & 1));
+            if (!ok || __any_sync(0xffffffffu, aborted(s_abort))) {
+                if (lane == 0 && !ok) {
+                    record_error(p.err, kErrEpilogueTimeout);
+                    atomicExch(s_abort, 1);
+                }
+                break;
+            }
+            ptx::tc_fence_after();
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
-                ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + 32 * c, r);
+                ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + b * BN + 32 * c, r);
                 ptx::tmem_ld_wait();
-                const int nb = n0 + 32 * c;
-                if (m >= p.m || nb >= p.n_out) continue;
-                __nv_bfloat16* drow = p.d + (size_t)m * p.ldd;
-                const __nv_bfloat16* crow = p.c ? p.c + (size_t)m * p.ldc : nullptr;
-#pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                    const int n = nb + 8 * g;
-                    float v[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) v[i] = p.alpha * __uint_as_float(r[8 * g + i]);
-                    const bool full8 = p.vec_store && n + 8 <= p.n_out;
-                    if (p.beta != 0.0f && crow) {
-                        if (full8) {
-                            const uint4 cv = *reinterpret_cast<const uint4*>(crow + n);
-                            const __nv_bfloat16* cb = reinterpret_cast<const __nv_bfloat16*>(&cv);
-#pragma unroll
-                            for (int i = 0; i < 8; ++i)
-                                v[i] = fmaf(p.alpha, __uint_as_float(r[8 * g + i]), p.beta * __bfloat162float(cb[i]));
-                        } else {
-                            for (int i = 0; i < 8 && n + i < p.n_out; ++i)
-                                v[i] = fmaf(p.alpha, __uint_as_float(r[8 * g + i]), p.beta * __bfloat162float(crow[n + i]));
-                        }
-                    }
-                    if (p.bias) {
-                        // Reference order: BF16 GEMM output, then a BF16 bias add.
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const float b = (n + i < p.n_out) ? __bfloat162float(p.bias[n + i]) : 0.0f;
-                            v[i] = __bfloat162float(__float2bfloat16_rn(v[i])) + b;
-                        }
-                    }
-                    if (full8) {
-                        uint4 o;
-                        o.x = bf16x2_bits(v[0], v[1]);
-                        o.y = bf16x2_bits(v[2], v[3]);
-                        o.z = bf16x2_bits(v[4], v[5]);
-                        o.w = bf16x2_bits(v[6], v[7]);
-                        *reinterpret_cast<uint4*>(drow + n) = o;
-                    } else {
-                        for (int i = 0; i < 8 && n + i < p.n_out; ++i) drow[n + i] = __float2bfloat16_rn(v[i]);
-                    }
+                if (c == BN / 32 - 1) {
+                    // All TMEM reads of this buffer are done: hand it back to the MMA warp.
+                    ptx::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive(&acc_empty[b]);
                 }
+                if (m < p.m && n0 + 32 * c < p.n_out) store_chunk(p, r, m, n0 + 32 * c);
             }
         }
     }
 
     ptx::tc_fence_before();
     __syncthreads();
-    if (threadIdx.x == 0 && *reinterpret_cast<volatile int*>(s_abort)) {
-        // Let every copy already issued land before the CTA's smem goes away.
-        const int last = *s_last_issued;
-        for (int ks = (last - STAGES + 1 > 0 ? last - STAGES + 1 : 0); ks <= last; ++ks)
-            ptx::mbar_wait(&full[ks % STAGES], (ks / STAGES) & 1);
-        ptx::mbar_wait(acc_full, 0);
+    if (threadIdx.x == 0) {
+        // Every MMA has completed before TMEM is released; on an abort, let the
+        // copies already issued land before the CTA's smem goes away.
+        ptx::mbar_wait(mma_done, 0);
+        if (aborted(s_abort)) {
+            const int last = *s_last_issued;
+            for (int k = (last - STAGES + 1 > 0 ? last - STAGES + 1 : 0); k <= last; ++k)
+                ptx::mbar_wait(&full[k % STAGES], (k / STAGES) & 1);
+        }
     }
     __syncthreads();
     if (warp == 1) {
@@ -308,12 +432,13 @@ EncodeTiledFn encode_fn() {
 }
 
 // Packed FP4 operand [rows, k_pad/2] bytes, 128-byte x box_rows boxes, 128B swizzle.
+// A box wholly or partly past K reads zeros (TMA out-of-bounds fill).
 bool make_operand_map(CUtensorMap* map, const void* base, long rows, long k_pad, int box_rows) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)(k_pad / 2), (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)(k_pad / 2)};
-    const cuuint32_t box[2] = {(cuuint32_t)kStageKBytes, (cuuint32_t)box_rows};
+    const cuuint32_t box[2] = {(cuuint32_t)kChunkBytes, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -352,8 +477,9 @@ cudaError_t launch_tile(const GemmArgs& g, cudaStream_t stream, int sms) {
     const bool d_al = (reinterpret_cast<uintptr_t>(g.d) & 15) == 0 && g.ldd % 8 == 0;
     const bool c_al = !g.c || ((reinterpret_cast<uintptr_t>(g.c) & 15) == 0 && g.ldc % 8 == 0);
     p.vec_store = (d_al && c_al) ? 1 : 0;
-    (void)sms;
-    dim3 grid((unsigned)((g.n_out + BN - 1) / BN), (unsigned)((g.m + kBM - 1) / kBM));
+    p.n_tiles = (int)((g.n_out + BN - 1) / BN);
+    p.num_tiles = p.n_tiles * (int)((g.m + kBM - 1) / kBM);
+    const int grid = p.num_tiles < sms ? p.num_tiles : sms;
     kernel<<<grid, kThreads, C::SMEM_BYTES, stream>>>(ma, mb, p);
     return cudaGetLastError();
 }
@@ -399,9 +525,9 @@ cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     const char* force = getenv("FP4B_FORCE_BN");
     const int bn = force ? atoi(force) : choose_bn(g.m, g.n_out, sms);
     switch (bn) {
-        case 256: return launch_tile<256, 4>(g, stream, sms);
-        case 192: return launch_tile<192, 4>(g, stream, sms);
-        case 128: return launch_tile<128, 6>(g, stream, sms);
+        case 256: return launch_tile<256, 2>(g, stream, sms);
+        case 192: return launch_tile<192, 2>(g, stream, sms);
+        case 128: return launch_tile<128, 3>(g, stream, sms);
         default: return cudaErrorInvalidValue;
     }
 }
