@@ -184,6 +184,13 @@ int read_and_clear_device_error() {
     return v;
 }
 
+bool cache_view(const void* handle, CacheView* out) {
+    WeightCache* c = as_cache(handle);
+    if (!c) return false;
+    *out = CacheView{c->fp4, c->sf, c->N, c->K};
+    return true;
+}
+
 void set_last_error(const char* fmt, ...) {
     va_list ap;
     va_start(ap, fmt);

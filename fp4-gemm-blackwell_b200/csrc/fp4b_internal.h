@@ -43,6 +43,15 @@ struct GemmArgs {
 const char* gemm_check(const GemmArgs& g);
 cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream);
 
+// Read-only view of a weight-cache handle created by the C ABI.
+struct CacheView {
+    const uint8_t* fp4;
+    const uint8_t* sf;
+    int N, K;
+};
+// False for a null or foreign handle.
+bool cache_view(const void* handle, CacheView* out);
+
 // Device-side error word written by kernels that gave up on a bounded wait.
 int* device_error_word();
 int read_and_clear_device_error();

@@ -157,6 +157,20 @@ int fp4b_weight_cache_export(const void* cache_handle, void* dst_fp4, void* dst_
  * `stream`.  NULL on failure. */
 void* fp4b_weight_cache_import(const void* src_fp4, const void* src_sf, int N, int K, void* stream);
 
+/* fp4b_run_cached_ex without any device allocation (no counterpart in the
+ * reference).  For callers that may not let a library allocate: a serving
+ * engine that has given nearly all of HBM to its own allocator, or a pipeline
+ * that cannot take the device-wide wait that cudaFree implies.  The quantized
+ * activations go to a fixed 9 MiB array that is part of the library's device
+ * code (16 Mi padded elements: round_up(m,128) * the cache's K must not exceed
+ * 16777216, else -1 with a message).  The first call on a device looks up that
+ * array's device address, so make it before capturing work into a CUDA graph.
+ * All calls on a device share the array: calls that overlap on the GPU race.
+ * Arguments, results and return codes as fp4b_run_cached_ex. */
+int fp4b_run_cached_noalloc(const void* A_bf16, int m, int k_in, int lda, const void* cache_handle, int n_out,
+                            const void* C_bf16, int ldc, void* D_bf16, int ldd, const void* bias_bf16, float alpha,
+                            float beta, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
