@@ -1,0 +1,76 @@
+"""Multi-GPU cached linear on one node (NCCL): column-parallel N-shards with an
+all-gather, and the data-parallel row split, against the single-GPU result.
+Runs as child processes on 2 GPUs; skipped on a 1-GPU box."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        import fp4_gemm
+        import fp4_gemm_dist as D
+        from tests import workloads as W
+        from tests.gpu_helpers import assert_gemm_close
+        m, n, k = 512, 2880, 1024
+        x, w, b = W.cached_linear_inputs(m, n, k, seed=3)
+        xd, wd, bd = x.to(dev), w.to(dev), b.to(dev)
+        tp = D.ColumnParallelFP4Linear(wd, bd)
+        y = tp.forward(xd)
+        single = fp4_gemm.FP4WeightCache(wd, bd)
+        ref = single.forward(xd)
+        assert_gemm_close(y, ref.float(), f"column-parallel rank {rank}")
+        r0, r1 = D.row_range(m, world, rank)
+        dp = D.DataParallelFP4Linear(wd, bd)
+        yl = dp.forward(xd[r0:r1], sync=True)
+        assert_gemm_close(yl, ref[r0:r1].float(), f"data-parallel rank {rank}")
+        tp.free()
+        dp.free()
+        single.free()
+        torch.cuda.synchronize()
+        dist.barrier()
+        q.put((rank, "ok"))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_column_and_data_parallel_two_gpus(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.exitcode is None:
+            p.kill()
+    results = [q.get(timeout=10) for _ in procs] if all(c == 0 for c in codes) else []
+    assert codes == [0, 0], f"rank exit codes {codes}"
+    assert all(r == "ok" for _, r in results), results
