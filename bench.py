@@ -7,9 +7,12 @@ M x N x K = 2048 x 2880 x 7680 (configs[1]; BF16 activations ~N(0,1), weights
 HBM GB/s on the config-4 tensor (16384 x 16384 Student-t stress input).
 
 A step = one cached linear call: quantize the activations + block-scaled GEMM
-with the fused bias, on inputs already in HBM.  L2 (126 MB > the 55 MB
-working set) is flushed by writing a 256 MiB buffer before every timed step;
-each step is timed alone with CUDA events on the launching stream.
+with the fused bias, on inputs already in HBM.  One step's working set (55 MB)
+fits in L2 (126 MB), so the timed loop rotates through enough independent
+input/weight/output sets to move more than twice L2 per pass ("inputs larger
+than L2"); K steps run back to back between one pair of CUDA events on the
+launching stream (an event pair per step would add ~4 us of event overhead to
+every step on this GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -120,22 +123,35 @@ class ClockSampler:
 
 # ------------------------------------------------------------------------------ timing
 class L2Flusher:
+    """Evicts L2 (126 MB) before a timed step: writes one 256 MiB buffer, then
+    reads another, so the timed step starts cold and with no dirty lines whose
+    write-back would overlap it."""
+
     def __init__(self, dev, mib: int = 256):
-        self.buf = torch.empty(mib * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+        n = mib * 1024 * 1024 // 4
+        self.wbuf = torch.empty(n, dtype=torch.float32, device=dev)
+        self.rbuf = torch.ones(n, dtype=torch.float32, device=dev)
+        self.out = torch.empty((), dtype=torch.float32, device=dev)
 
     def __call__(self):
-        self.buf.fill_(1.0)
+        self.wbuf.fill_(1.0)
+        torch.amax(self.rbuf, dim=0, out=self.out)
 
 
 def time_launches(fn, steps: int, warmup: int, flush=None, stream=None) -> list[float]:
-    """Per-call device milliseconds (CUDA events on `stream`), L2 flushed before each."""
+    """Per-call device milliseconds (CUDA events on `stream`), L2 flushed before each.
+
+    The GPU is first parked on a sleep kernel long enough for the host to
+    enqueue every timed call, so the events measure device time only, never a
+    gap in which the GPU waits for Python to launch the next kernel."""
     stream = stream or torch.cuda.current_stream()
     for _ in range(warmup):
         if flush:
             flush()
         fn()
     torch.cuda.synchronize()
-    times = []
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(int(2e6) * (steps + 10))  # ~1 ms of device time per step queued behind it
     pairs = []
     for _ in range(steps):
         if flush:
@@ -146,9 +162,36 @@ def time_launches(fn, steps: int, warmup: int, flush=None, stream=None) -> list[
         e.record(stream)
         pairs.append((s, e))
     torch.cuda.synchronize()
-    for s, e in pairs:
-        times.append(s.elapsed_time(e))
-    return times
+    return [s.elapsed_time(e) for s, e in pairs]
+
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+def sets_needed(bytes_per_set: int) -> int:
+    """Distinct buffer sets so that one pass over them moves more than twice L2."""
+    return max(2, -(-2 * L2_BYTES // max(1, bytes_per_set)))
+
+
+def time_rotating(fns, steps: int, warmup: int, stream=None) -> float:
+    """Average device milliseconds per call of K back-to-back calls, call i
+    using buffer set i % len(fns); the sets together exceed L2, so every call
+    reads its inputs from HBM.  One CUDA-event pair brackets the K calls (an
+    event pair per call would add ~4 us of event overhead to each), and the
+    GPU is parked on a sleep while the host enqueues them."""
+    stream = stream or torch.cuda.current_stream()
+    for i in range(warmup):
+        fns[i % len(fns)]()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(int(2e6) * (steps + 10))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(steps):
+        fns[i % len(fns)]()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
 
 
 # ------------------------------------------------------------------------------ CPU reference path
@@ -246,6 +289,8 @@ def run_reference_arm(args):
 
 # ------------------------------------------------------------------------------ our arm
 def run_ours(args):
+    import datetime
+
     import torch.distributed as dist
 
     import fp4_gemm
@@ -255,71 +300,75 @@ def run_ours(args):
     if ws > 1:
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local),
-                                timeout=__import__("datetime").timedelta(seconds=300))
+                                timeout=datetime.timedelta(seconds=300))
     dev = torch.device("cuda", local if ws > 1 else 0)
     torch.cuda.set_device(dev)
     peaks = load_peaks()
     fp4_peak = 4.0 * peaks["bf16_tflops"]
-
-    m, n, k = W.HEADLINE_SHAPE
-    x, w, b = W.cached_linear_inputs(m, n, k, seed=rank)
-    xd, wd, bd = x.to(dev), w.to(dev), b.to(dev)
-    cache = fp4_gemm.FP4WeightCache(wd, bd)
-    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
-    flush = L2Flusher(dev)
     lib = fp4_gemm._lib
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
 
-    def step():
-        rc = lib.fp4b_run_cached_ex(xd.data_ptr(), m, k, k, cache._handle, n, None, 0, out.data_ptr(), n,
-                                    bd.data_ptr(), 1.0, 0.0, sptr)
-        if rc != 0:
-            raise RuntimeError(f"cached linear failed: {rc} {fp4_gemm._last_error()}")
+    # --- headline: cached linear 2048 x 2880 x 7680 + bias, buffer sets rotated past L2
+    m, n, k = W.HEADLINE_SHAPE
+    per_set = m * k * 2 + (n + 64) * k * 9 // 16 + m * n * 2 + m * k * 9 // 16
+    nsets = sets_needed(per_set)
+    sets = []
+    for i in range(nsets):
+        x, w, b = W.cached_linear_inputs(m, n, k, seed=1000 * rank + i)
+        xd, bd = x.to(dev), b.to(dev)
+        cache = fp4_gemm.FP4WeightCache(w.to(dev), bd)
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        aq, asf = fp4_gemm.quantize_to_buffers(xd, None, cache.K)
+        sets.append(dict(x=xd, b=bd, cache=cache, out=out, aq=aq, asf=asf, wsd=cache.state_dict()))
 
-    # kernel-level pieces for the roofline: quantize of A alone, GEMM alone
-    k_pad = cache.K
-    aq, asf = fp4_gemm.quantize_to_buffers(xd, None, k_pad)
-    wsd = cache.state_dict()
+    def make_step(st):
+        def step():
+            rc = lib.fp4b_run_cached_ex(st["x"].data_ptr(), m, k, k, st["cache"]._handle, n, None, 0,
+                                        st["out"].data_ptr(), n, st["b"].data_ptr(), 1.0, 0.0, sptr)
+            if rc != 0:
+                raise RuntimeError(f"cached linear failed: {rc} {fp4_gemm._last_error()}")
+        return step
 
-    def quant_only():
-        lib.fp4b_quantize(xd.data_ptr(), m, k, k, aq.data_ptr(), asf.data_ptr(), aq.shape[0], k_pad, sptr)
+    def make_gemm(st):
+        kp = st["cache"].K
+        return lambda: lib.fp4b_gemm_prequant(st["aq"].data_ptr(), st["asf"].data_ptr(), m, st["aq"].shape[0],
+                                              st["wsd"]["fp4"].data_ptr(), st["wsd"]["sf"].data_ptr(), n,
+                                              st["cache"].N, kp, None, 0, st["out"].data_ptr(), n,
+                                              st["b"].data_ptr(), 1.0, 0.0, sptr)
 
-    def gemm_only():
-        lib.fp4b_gemm_prequant(aq.data_ptr(), asf.data_ptr(), m, aq.shape[0], wsd["fp4"].data_ptr(),
-                               wsd["sf"].data_ptr(), n, cache.N, k_pad, None, 0, out.data_ptr(), n, bd.data_ptr(),
-                               1.0, 0.0, sptr)
+    def make_quant(st):
+        kp = st["cache"].K
+        return lambda: lib.fp4b_quantize(st["x"].data_ptr(), m, k, k, st["aq"].data_ptr(), st["asf"].data_ptr(),
+                                         st["aq"].shape[0], kp, sptr)
 
+    steps_fns = [make_step(st) for st in sets]
     clocks = ClockSampler(dev.index if ws == 1 else local)
     clocks.start()
     if ws > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    step_ms = time_launches(step, args.steps, args.warmup, flush, stream)
+    ms_per_step = time_rotating(steps_fns, args.steps, args.warmup, stream)
     torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
-    gemm_ms = time_launches(gemm_only, args.steps, args.warmup, flush, stream)
-    quant_ms = time_launches(quant_only, args.steps, args.warmup, flush, stream)
+    gemm_ms = time_rotating([make_gemm(st) for st in sets], args.steps, args.warmup, stream)
+    quant_ms = time_rotating([make_quant(st) for st in sets], args.steps, args.warmup, stream)
     clk = clocks.stop()
 
-    total_step_ms = sum(step_ms)
     if ws > 1:
-        t = torch.tensor([total_step_ms], device=dev, dtype=torch.float64)
+        t = torch.tensor([ms_per_step], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_step_ms = float(t.item())
-    ms_per_step = total_step_ms / args.steps
+        ms_per_step = float(t.item())
     flops = 2.0 * m * n * k
     value = ws * flops / (ms_per_step * 1e-3) / 1e12
-
-    gemm_avg = sum(gemm_ms) / len(gemm_ms)
-    quant_avg = sum(quant_ms) / len(quant_ms)
-    gemm_tflops = flops / (gemm_avg * 1e-3) / 1e12
-    quant_bytes = m * k * 2 + aq.shape[0] * k_pad // 2 + aq.shape[0] * k_pad // 16
+    gemm_tflops = flops / (gemm_ms * 1e-3) / 1e12
+    aq0 = sets[0]["aq"]
+    quant_bytes = m * k * 2 + aq0.shape[0] * aq0.shape[1] + aq0.shape[0] * aq0.shape[1] // 8
 
     result = None
     if rank == 0:
-        # standalone quantizer, config 4 (input 512 MiB > L2, no flush needed)
+        # standalone quantizer, config 4 (input 512 MiB > L2)
         q4 = W.quantizer_stress(16384, 16384, seed=0).to(dev)
         q4_fp4 = torch.empty(16384, 8192, dtype=torch.uint8, device=dev)
         q4_sf = torch.empty(16384 * 1024, dtype=torch.uint8, device=dev)
@@ -327,37 +376,40 @@ def run_ours(args):
         def quant4():
             lib.fp4b_quantize(q4.data_ptr(), 16384, 16384, 16384, q4_fp4.data_ptr(), q4_sf.data_ptr(), 16384,
                               16384, sptr)
-        q4_ms = time_launches(quant4, max(10, args.steps // 2), 3, None, stream)
+        q4_ms = time_rotating([quant4], max(10, args.steps // 2), 3, stream)
         q4_bytes = 16384 * 16384 * (2 + 0.5 + 0.0625)
-        q4_gbs = q4_bytes / (statistics.mean(q4_ms) * 1e-3) / 1e9
+        q4_gbs = q4_bytes / (q4_ms * 1e-3) / 1e9
         del q4, q4_fp4, q4_sf
 
         # shape sweep of configs[1] (and config 1), cached linear with bias
         sweep = {}
-        for (sm_, sn, sk) in [W.CFG1_SHAPE] + [s for s in W.CACHED_SHAPES if s != W.HEADLINE_SHAPE]:
-            sx, sw, sb = W.cached_linear_inputs(sm_, sn, sk, seed=1)
-            sxd, sbd = sx.to(dev), sb.to(dev)
-            sc = fp4_gemm.FP4WeightCache(sw.to(dev), sbd)
-            so = torch.empty(sm_, sn, dtype=torch.bfloat16, device=dev)
+        for (sm_, sn, sk) in [W.CFG1_SHAPE] + [sh for sh in W.CACHED_SHAPES if sh != W.HEADLINE_SHAPE]:
+            sbytes = sm_ * sk * 2 + sn * sk * 9 // 16 + sm_ * sn * 2
+            ssets = []
+            for i in range(sets_needed(sbytes)):
+                sx, sw, sb = W.cached_linear_inputs(sm_, sn, sk, seed=2000 + i)
+                ssets.append((sx.to(dev), fp4_gemm.FP4WeightCache(sw.to(dev), sb.to(dev)), sb.to(dev),
+                              torch.empty(sm_, sn, dtype=torch.bfloat16, device=dev)))
 
-            def sstep():
-                lib.fp4b_run_cached_ex(sxd.data_ptr(), sm_, sk, sk, sc._handle, sn, None, 0, so.data_ptr(), sn,
-                                       sbd.data_ptr(), 1.0, 0.0, sptr)
-            st = time_launches(sstep, max(10, args.steps // 2), 3, flush, stream)
-            ms = statistics.mean(st)
-            sweep[f"{sm_}x{sn}x{sk}"] = {"ms": ms, "tflops": 2.0 * sm_ * sn * sk / (ms * 1e-3) / 1e12}
-            sc.free()
+            def mk(t):
+                sxd, sc, sbd, so = t
+                return lambda: lib.fp4b_run_cached_ex(sxd.data_ptr(), sm_, sk, sk, sc._handle, sn, None, 0,
+                                                      so.data_ptr(), sn, sbd.data_ptr(), 1.0, 0.0, sptr)
+            sms_ = time_rotating([mk(t) for t in ssets], max(10, args.steps // 2), 3, stream)
+            sweep[f"{sm_}x{sn}x{sk}"] = {"ms": sms_, "tflops": 2.0 * sm_ * sn * sk / (sms_ * 1e-3) / 1e12}
+            for t in ssets:
+                t[1].free()
 
-        # end to end through the public API: pinned host in, pinned host out
-        x_host = x.pin_memory()
+        # end to end through the public API: pinned host in, pinned host out, every step
+        x_host = W.cached_linear_inputs(m, n, k, seed=0)[0].pin_memory()
         y_host = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+        cache0 = sets[0]["cache"]
 
         def e2e_step():
             xg = x_host.to(dev, non_blocking=True)
-            y = cache.forward(xg, sync=False)
+            y = cache0.forward(xg, sync=False)
             y_host.copy_(y, non_blocking=True)
-        e2e_ms = time_launches(e2e_step, args.steps, args.warmup, flush, stream)
-        e2e_avg = statistics.mean(e2e_ms)
+        e2e_ms = time_rotating([e2e_step], args.steps, args.warmup, stream)
 
         cpu = cpu_baseline(m, n, k) if ws == 1 else None
         traffic = None
@@ -381,11 +433,13 @@ def run_ours(args):
             "config": {"workload": f"cached-linear {m}x{n}x{k} + bias (configs[1]); quantize activations + "
                                    "tcgen05 block-scaled GEMM per step, weights quantized once",
                        "M": m, "N": n, "K": k, "parallelism": f"dp{ws} (M-split, no collective)",
-                       "l2": "flushed (256 MiB write) before every timed step"},
-            "pct_fp4_peak_datasheet": 100.0 * value / FP4_DATASHEET_TFLOPS,
+                       "l2": f"inputs larger than L2: {nsets} independent input/weight/output sets rotated "
+                             f"({nsets * per_set / 2**20:.0f} MiB per pass), K steps back to back"},
+            "pct_fp4_peak_datasheet": 100.0 * (value / ws) / FP4_DATASHEET_TFLOPS,
             "pct_fp4_peak_4x_measured_bf16": 100.0 * (value / ws) / fp4_peak,
-            "kernels": {"quantize_activations_us": quant_avg * 1e3, "gemm_us": gemm_avg * 1e3,
-                        "step_us": ms_per_step * 1e3, "quantize_activations_gbs": quant_bytes / (quant_avg * 1e-3) / 1e9},
+            "kernels": {"quantize_activations_us": quant_ms * 1e3, "gemm_us": gemm_ms * 1e3,
+                        "step_us": ms_per_step * 1e3,
+                        "quantize_activations_gbs": quant_bytes / (quant_ms * 1e-3) / 1e9},
             "roofline": {"bound": "tensor", "kernel": "nvf4_gemm_kernel (2048x2880x7680)",
                          "achieved": gemm_tflops, "peak": fp4_peak, "unit": "TFLOP/s",
                          "frac": gemm_tflops / fp4_peak, "traffic": traffic,
@@ -393,12 +447,11 @@ def run_ours(args):
                                         "B200 dense FP4 = 4 x dense BF16",
                          "frac_of_datasheet_9pf": gemm_tflops / FP4_DATASHEET_TFLOPS},
             "quantize": {"workload": "config 4: 16384x16384 bf16 Student-t stress, bit-exact",
-                         "value": q4_gbs, "unit": "GB/s", "ms": statistics.mean(q4_ms),
+                         "value": q4_gbs, "unit": "GB/s", "ms": q4_ms,
                          "roofline": {"bound": "hbm", "achieved": q4_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                                      "frac": q4_gbs / peaks["hbm_gbs"],
-                                      "algorithmic_bytes": q4_bytes}},
+                                      "frac": q4_gbs / peaks["hbm_gbs"], "algorithmic_bytes": q4_bytes}},
             "sweep": sweep,
-            "e2e": {"value": flops / (e2e_avg * 1e-3) / 1e12, "unit": "TFLOPS",
+            "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
                     "h2d_bytes_per_step": m * k * 2, "d2h_bytes_per_step": m * n * 2,
                     "path": "fp4_gemm.FP4WeightCache.forward(sync=False) with pinned host in/out copies"},
             "gpu_launches": 2 * args.steps,
@@ -406,7 +459,8 @@ def run_ours(args):
         }
         if cpu is not None:
             result["cpu_baseline"] = cpu
-    cache.free()
+    for st in sets:
+        st["cache"].free()
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()

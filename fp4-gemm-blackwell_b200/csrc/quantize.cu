@@ -5,7 +5,9 @@
 //   * one thread per 16-element block, flattened (row, block) index so a warp
 //     reads 1 KB of contiguous BF16 with two 16-byte loads per thread;
 //   * |x|max as an integer max over the bf16 bit patterns (exact for finite
-//     values), scale = IEEE absmax/6 -> UE4M3 encode -> reciprocal table;
+//     values); absmax/6 rounded to nearest from a 128-entry table of
+//     RN((128 + m) / 6) scaled by the exponent (exact for normal results);
+//     UE4M3 encode; reciprocal table;
 //   * E2M1 rounding by a 2048-entry shared-memory table indexed by
 //     (bits(x*inv) - 1) >> 21, which reproduces the reference's strict-<
 //     nearest-value scan (ties to the lower code, sign for any value < 0)
@@ -17,6 +19,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <mutex>
 
 #include "fp4b_internal.h"
 #include "nvfp4_codec.cuh"
@@ -28,7 +31,11 @@ namespace {
 struct QuantTables {
     uint8_t e2m1[kE2M1TableSize];  // code by fp32 bit slot
     float rcp[128];                // 1 / ue4m3_decode(byte), IEEE round-to-nearest
+    uint32_t div6[128];            // bits of RN((128 + m) / 6) for a bf16 mantissa m
 };
+
+// |x|max (bf16 bits) below 6 * 2^-9 gives absmax/6 < 2^-9: the scale clamps to 0x01.
+constexpr uint32_t kScaleClampBf16 = 0x3C40u;
 
 struct QuantParams {
     const uint16_t* src;
@@ -42,12 +49,20 @@ struct QuantParams {
     uint32_t vec_ok;   // 16-byte aligned rows
 };
 
+// Device copy of the tables, written once per device (host_tables() -> here).
+// Read with coalesced loads at CTA start; passing them as kernel parameters
+// instead cost several microseconds per CTA (divergent constant-bank reads).
+__device__ QuantTables g_qtab;
+std::mutex g_qtab_mu;
+bool g_qtab_ready[64];
+
 // Tables built on the host from the same codec definitions as the device code.
 const QuantTables& host_tables() {
     static const QuantTables t = [] {
         QuantTables q{};
         for (uint32_t i = 0; i < (uint32_t)kE2M1TableSize; ++i) q.e2m1[i] = e2m1_table_entry(i);
         for (int b = 0; b < 128; ++b) q.rcp[b] = 1.0f / ue4m3_decode((uint8_t)b);
+        for (int m = 0; m < 128; ++m) q.div6[m] = f32_bits((float)(128 + m) / 6.0f);
         return q;
     }();
     return t;
@@ -120,69 +135,93 @@ __device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
 }
 
 constexpr int kThreads = 256;
+constexpr int kBlocksPerThread = 2;  // 16-element blocks per thread per loop trip
 
-__global__ void __launch_bounds__(kThreads) nvfp4_quantize_kernel(const __grid_constant__ QuantParams p,
-                                                                  const __grid_constant__ QuantTables tabs) {
+// Scale byte of a block from its |x|max (bf16 bits < kFastAbsmaxBf16Limit):
+// RN(absmax / 6) = RN((128 + m) / 6) * 2^(E - 134) exactly while the result is
+// a normal fp32, which it is whenever absmax / 6 >= 2^-9; below that the
+// reference clamps to 2^-9 (byte 0x01).
+__device__ __forceinline__ uint32_t scale_byte(uint32_t amax_bits, const uint32_t* div6) {
+    if (amax_bits < kScaleClampBf16) return 0x01u;
+    const uint32_t s_bits = div6[amax_bits & 0x7Fu] + (((amax_bits >> 7) - 134u) << 23);
+    return ue4m3_encode(__uint_as_float(s_bits));
+}
+
+__device__ __forceinline__ void load_block(const QuantParams& p, uint32_t idx, uint32_t (&w)[8], uint32_t& r,
+                                           uint32_t& kb) {
+    const bool valid = idx < p.total;
+    r = (__umulhi(idx, p.div_mul) + idx) >> p.div_shift;
+    kb = idx - r * p.nsb;
+    const uint32_t c0 = kb * kSfVec;
+    if (valid && p.vec_ok && r < p.rows && c0 + kSfVec <= p.cols) {
+        const uint4* g = reinterpret_cast<const uint4*>(p.src + (size_t)r * p.ld + c0);
+        const uint4 v0 = __ldcs(g);
+        const uint4 v1 = __ldcs(g + 1);
+        w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
+        w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
+    } else {
+        // Ragged edge, padding rows/columns or unaligned rows: element loads, zeros outside.
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[i] = valid ? load_pair(p.src, p.ld, p.rows, p.cols, r, c0 + 2 * i) : 0u;
+    }
+}
+
+__device__ __forceinline__ void quantize_and_store(const QuantParams& p, uint32_t idx, const uint32_t (&w)[8],
+                                                   uint32_t r, uint32_t kb, uint32_t lane, const uint8_t* s_e2m1,
+                                                   const float* s_rcp, const uint32_t* s_div6) {
+    uint32_t mx = w[0] & 0x7FFF7FFFu;
+#pragma unroll
+    for (int i = 1; i < 8; ++i) mx = max_u16x2(mx, w[i] & 0x7FFF7FFFu);
+    const uint32_t amax_bits = max(mx & 0xFFFFu, mx >> 16);
+
+    uint32_t sbyte, out0 = 0, out1 = 0;
+    if (amax_bits < kFastAbsmaxBf16Limit) {
+        sbyte = scale_byte(amax_bits, s_div6);
+        const float inv = s_rcp[sbyte];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            out0 |= pack_pair_fast(w[i], inv, s_e2m1) << (8 * i);
+            out1 |= pack_pair_fast(w[i + 4], inv, s_e2m1) << (8 * i);
+        }
+    } else {
+        quantize_block_exact(p.src, p.ld, p.rows, p.cols, r, kb * kSfVec, s_rcp, &sbyte, &out0, &out1);
+    }
+    const bool valid = idx < p.total;
+    if (valid) *reinterpret_cast<uint2*>(p.fp4 + (size_t)idx * 8) = make_uint2(out0, out1);
+
+    // Scales of 4 consecutive blocks of one row are 4 consecutive bytes.
+    uint32_t sw = sbyte << (8 * (lane & 3u));
+    sw |= __shfl_xor_sync(0xffffffffu, sw, 1);
+    sw |= __shfl_xor_sync(0xffffffffu, sw, 2);
+    if (valid && (lane & 3u) == 0) *reinterpret_cast<uint32_t*>(p.sf + sf_offset(r, kb, p.nsb)) = sw;
+}
+
+__global__ void __launch_bounds__(kThreads) nvfp4_quantize_kernel(const __grid_constant__ QuantParams p) {
     __shared__ __align__(16) uint8_t s_e2m1[kE2M1TableSize];
     __shared__ float s_rcp[128];
+    __shared__ uint32_t s_div6[128];
     {
-        const uint4* src = reinterpret_cast<const uint4*>(tabs.e2m1);
+        const uint4* src = reinterpret_cast<const uint4*>(g_qtab.e2m1);
         uint4* dst = reinterpret_cast<uint4*>(s_e2m1);
-        for (int i = threadIdx.x; i < kE2M1TableSize / 16; i += kThreads) dst[i] = src[i];
-        if (threadIdx.x < 128) s_rcp[threadIdx.x] = tabs.rcp[threadIdx.x];
+        for (int i = threadIdx.x; i < kE2M1TableSize / 16; i += kThreads) dst[i] = __ldg(src + i);
+        if (threadIdx.x < 128) {
+            s_rcp[threadIdx.x] = __ldg(&g_qtab.rcp[threadIdx.x]);
+            s_div6[threadIdx.x] = __ldg(&g_qtab.div6[threadIdx.x]);
+        }
     }
     __syncthreads();
 
     const uint32_t lane = threadIdx.x & 31u;
-    const uint32_t stride = gridDim.x * kThreads;
-    for (uint32_t base = blockIdx.x * kThreads; base < p.total; base += stride) {
-        const uint32_t idx = base + threadIdx.x;
-        const bool valid = idx < p.total;
-        const uint32_t r = (__umulhi(idx, p.div_mul) + idx) >> p.div_shift;
-        const uint32_t kb = idx - r * p.nsb;
-        const uint32_t c0 = kb * kSfVec;
-
-        uint32_t w[8];
-        if (valid && p.vec_ok && r < p.rows && c0 + kSfVec <= p.cols) {
-            const uint4* g = reinterpret_cast<const uint4*>(p.src + (size_t)r * p.ld + c0);
-            const uint4 v0 = __ldcs(g);
-            const uint4 v1 = __ldcs(g + 1);
-            w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
-            w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
-        } else {
-            // Ragged edge, padding rows/columns or unaligned rows: element loads, zeros outside.
-#pragma unroll
-            for (int i = 0; i < 8; ++i) w[i] = valid ? load_pair(p.src, p.ld, p.rows, p.cols, r, c0 + 2 * i) : 0u;
-        }
-
-        uint32_t mx = w[0] & 0x7FFF7FFFu;
-#pragma unroll
-        for (int i = 1; i < 8; ++i) mx = max_u16x2(mx, w[i] & 0x7FFF7FFFu);
-        const uint32_t amax_bits = max(mx & 0xFFFFu, mx >> 16);
-
-        uint32_t sbyte, out0 = 0, out1 = 0;
-        if (amax_bits < kFastAbsmaxBf16Limit) {
-            float s = __fdiv_rn(__uint_as_float(amax_bits << 16), 6.0f);
-            if (s < kScaleMin) s = kScaleMin;
-            sbyte = ue4m3_encode(s);
-            const float inv = s_rcp[sbyte];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                out0 |= pack_pair_fast(w[i], inv, s_e2m1) << (8 * i);
-                out1 |= pack_pair_fast(w[i + 4], inv, s_e2m1) << (8 * i);
-            }
-        } else {
-            quantize_block_exact(p.src, p.ld, p.rows, p.cols, r, c0, s_rcp, &sbyte, &out0, &out1);
-        }
-
-        if (valid) *reinterpret_cast<uint2*>(p.fp4 + (size_t)idx * 8) = make_uint2(out0, out1);
-
-        // Scales of 4 consecutive blocks of one row are 4 consecutive bytes.
-        uint32_t sw = sbyte << (8 * (lane & 3u));
-        sw |= __shfl_xor_sync(0xffffffffu, sw, 1);
-        sw |= __shfl_xor_sync(0xffffffffu, sw, 2);
-        if (valid && (lane & 3u) == 0)
-            *reinterpret_cast<uint32_t*>(p.sf + sf_offset(r, kb, p.nsb)) = sw;
+    constexpr uint32_t kSpan = kThreads * kBlocksPerThread;
+    const uint32_t stride = gridDim.x * kSpan;
+    for (uint32_t base = blockIdx.x * kSpan; base < p.total; base += stride) {
+        // Both loads are issued before either block is processed.
+        const uint32_t i0 = base + threadIdx.x, i1 = i0 + kThreads;
+        uint32_t w0[8], w1[8], r0, kb0, r1, kb1;
+        load_block(p, i0, w0, r0, kb0);
+        load_block(p, i1, w1, r1, kb1);
+        quantize_and_store(p, i0, w0, r0, kb0, lane, s_e2m1, s_rcp, s_div6);
+        quantize_and_store(p, i1, w1, r1, kb1, lane, s_e2m1, s_rcp, s_div6);
     }
 }
 
@@ -218,10 +257,20 @@ cudaError_t quantize_launch(const QuantizeArgs& a, cudaStream_t stream) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const uint32_t need = (p.total + kThreads - 1) / kThreads;
+    {
+        // First use on this device: copy the tables (synchronous, not an allocation).
+        std::lock_guard<std::mutex> lk(g_qtab_mu);
+        if (!g_qtab_ready[dev & 63]) {
+            const cudaError_t e = cudaMemcpyToSymbol(g_qtab, &host_tables(), sizeof(QuantTables));
+            if (e != cudaSuccess) return e;
+            g_qtab_ready[dev & 63] = true;
+        }
+    }
+    const uint32_t span = kThreads * kBlocksPerThread;
+    const uint32_t need = (p.total + span - 1) / span;
     const uint32_t cap = (uint32_t)sms * 8u;
     const uint32_t grid = need < cap ? need : cap;
-    nvfp4_quantize_kernel<<<grid, kThreads, 0, stream>>>(p, host_tables());
+    nvfp4_quantize_kernel<<<grid, kThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -89,3 +89,25 @@ def test_scale_layout_is_bijective():
         nsb = k // 16
         offs = {O.sf_index(r, kb, nsb) for r in range(rows) for kb in range(nsb)}
         assert offs == set(range(rows * nsb))
+
+
+def test_division_table_matches_ieee_for_every_bf16_absmax():
+    # The GPU kernel forms RN(absmax / 6) as RN((128 + m) / 6) * 2^(E - 134) for
+    # every fast-path |x|max (bf16 bits below 0x4E80) at or above 6 * 2^-9, and
+    # uses scale byte 0x01 below; the reference divides in IEEE fp32.
+    bits = np.arange(0, 0x4E80, dtype=np.uint32)
+    amax = (bits << 16).view(np.float32)
+    div6 = (np.arange(128, dtype=np.float32) + np.float32(128)) / np.float32(6)
+    hi = bits >= 0x3C40
+    e = (bits >> 7).astype(np.int64)
+    table = (div6.view(np.uint32)[bits & 0x7F].astype(np.int64) + ((e - 134) << 23)).astype(np.uint32)
+    ieee = (amax / np.float32(6)).astype(np.float32)
+    assert np.array_equal(table[hi].view(np.float32), ieee[hi])
+    assert np.all(ieee[~hi] <= np.float32(2.0 ** -9))
+    # and the resulting scale bytes, through the oracle's encoder
+    s_ref = np.maximum(ieee, np.float32(2.0 ** -9))
+    sample = np.concatenate([np.arange(0, 0x4E80, 7), [0x3C3F, 0x3C40, 0x3C41, 0x4E7F]])
+    for b in sample:
+        want = O.ue4m3_encode(float(s_ref[b]))
+        got = 0x01 if b < 0x3C40 else O.ue4m3_encode(float(table[b].view(np.float32)))
+        assert got == want, hex(b)
