@@ -44,9 +44,6 @@ namespace {
 
 constexpr int kBM = 128;            // rows of A per tile (one tcgen05 M)
 constexpr int kChunkBytes = 128;    // one 128B-swizzle atom row: 256 FP4 elements of K
-constexpr int kChunks = 2;          // chunks per stage: a stage covers K = 512
-constexpr int kStageKBytes = kChunks * kChunkBytes;
-constexpr int kKbPerStage = 8;      // 64-element MMA k-blocks per stage
 constexpr int kAtomBytes = 512;     // 128 rows x 4 scale bytes
 constexpr int kThreads = 192;
 constexpr int kEpilogueWarps = 4;
@@ -68,8 +65,12 @@ constexpr int max_row_tiles(int bn) {
 // 128-row scale atom and the MMA's scale-B TMEM address moves by 0 or 2
 // columns.  An odd column (a tile starting 32 or 96 rows into an atom, e.g.
 // BN = 160) raised a misaligned-address error on B200.
-template <int BN, int STAGES>
+template <int BN, int STAGES, int CHUNKS>
 struct Cfg {
+    // CHUNKS 128-byte-wide chunks of K per stage: a stage covers K = 256 * CHUNKS.
+    static constexpr int kChunks = CHUNKS;
+    static constexpr int kStageKBytes = CHUNKS * kChunkBytes;
+    static constexpr int kKbPerStage = 4 * CHUNKS;  // 64-element MMA k-blocks per stage
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 64 in [64, 256]");
     static constexpr int NRT = max_row_tiles(BN);
     static constexpr int A_CHUNK = kBM * kChunkBytes;   // one TMA box
@@ -171,11 +172,14 @@ __device__ __forceinline__ void store_chunk(const Params& p, const uint32_t (&r)
 // Persistent kernel: CTA b processes tiles b, b + gridDim.x, ... (N fastest).
 // The smem ring and the TMEM accumulators carry across tiles, so loads of the
 // next tile and the epilogue of the previous one overlap the MMAs.
-template <int BN, int STAGES>
+template <int BN, int STAGES, int CHUNKS>
 __global__ void __launch_bounds__(kThreads, 1)
     nvf4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                      const __grid_constant__ Params p) {
-    using C = Cfg<BN, STAGES>;
+    using C = Cfg<BN, STAGES, CHUNKS>;
+    constexpr int kChunks = C::kChunks;
+    constexpr int kStageKBytes = C::kStageKBytes;
+    constexpr int kKbPerStage = C::kKbPerStage;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -260,15 +264,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (j == 0) ptx::mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES + sf_bytes * (1 + nrt));
                 __syncwarp();
                 const int kx = ks * kStageKBytes;
-                if (j == 0 || j == 1) {
+                if (j >= 0 && j < kChunks) {
                     ptx::tma_load_2d(sA + s * C::A_BYTES + j * C::A_CHUNK, &tmap_a, &full[s], kx + j * kChunkBytes, m0);
-                } else if (j == 2 || j == 3) {
-                    ptx::tma_load_2d(sB + s * C::B_BYTES + (j - 2) * C::B_CHUNK, &tmap_b, &full[s],
-                                     kx + (j - 2) * kChunkBytes, n0);
-                } else if (j == 4) {
+                } else if (j >= kChunks && j < 2 * kChunks) {
+                    ptx::tma_load_2d(sB + s * C::B_BYTES + (j - kChunks) * C::B_CHUNK, &tmap_b, &full[s],
+                                     kx + (j - kChunks) * kChunkBytes, n0);
+                } else if (j == 2 * kChunks) {
                     ptx::bulk_load(sSFA + s * C::SFA_BYTES, sfa_tile + (size_t)kb0 * kAtomBytes, sf_bytes, &full[s]);
-                } else if (j >= 5 && j < 5 + nrt) {
-                    const int rt = j - 5;
+                } else if (j > 2 * kChunks && j <= 2 * kChunks + nrt) {
+                    const int rt = j - 2 * kChunks - 1;
                     const uint8_t* src = p.b_sf + ((size_t)(rt0 + rt) * num_kb + kb0) * kAtomBytes;
                     ptx::bulk_load(sSFB + s * C::SFB_BYTES + rt * kKbPerStage * kAtomBytes, src, sf_bytes, &full[s]);
                 }
@@ -445,10 +449,10 @@ bool make_operand_map(CUtensorMap* map, const void* base, long rows, long k_pad,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int CHUNKS>
 cudaError_t launch_tile(const GemmArgs& g, cudaStream_t stream, int sms) {
-    using C = Cfg<BN, STAGES>;
-    auto kernel = nvf4_gemm_kernel<BN, STAGES>;
+    using C = Cfg<BN, STAGES, CHUNKS>;
+    auto kernel = nvf4_gemm_kernel<BN, STAGES, CHUNKS>;
     static std::once_flag attr_once[64];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -524,10 +528,12 @@ cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const char* force = getenv("FP4B_FORCE_BN");
     const int bn = force ? atoi(force) : choose_bn(g.m, g.n_out, sms);
+    const char* stages_env = getenv("FP4B_DEEP");
+    const bool deep = stages_env ? atoi(stages_env) != 0 : true;
     switch (bn) {
-        case 256: return launch_tile<256, 2>(g, stream, sms);
-        case 192: return launch_tile<192, 2>(g, stream, sms);
-        case 128: return launch_tile<128, 3>(g, stream, sms);
+        case 256: return deep ? launch_tile<256, 4, 1>(g, stream, sms) : launch_tile<256, 2, 2>(g, stream, sms);
+        case 192: return deep ? launch_tile<192, 4, 1>(g, stream, sms) : launch_tile<192, 2, 2>(g, stream, sms);
+        case 128: return deep ? launch_tile<128, 6, 1>(g, stream, sms) : launch_tile<128, 3, 2>(g, stream, sms);
         default: return cudaErrorInvalidValue;
     }
 }
