@@ -6,8 +6,10 @@
 // elements in the 128x4 interleaved layout (the layout tcgen05 wants, so the
 // scale bytes are copied to tensor memory as they are).
 //
-// Persistent kernel, one CTA per SM walking 128 x BN output tiles; 192
-// threads in three roles:
+// Two persistent kernels.  When A has more than 128 rows, CTA pairs (clusters
+// of two, tcgen05 cta_group::2) walk 256 x BN tiles; see the pair kernel
+// below.  Otherwise (and on request) one CTA per SM walks 128 x BN output
+// tiles with 192 threads in three roles:
 //   warp 0     TMA producer.  A stage covers K = 512: two 128-byte-wide TMA
 //              boxes (128B swizzle) for A, two for B, one bulk copy of the A
 //              scale atoms and one per 128-row tile of B scales, all
@@ -418,6 +420,299 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ------------------------------------------------------------------ CTA-pair kernel
+// 256 x BN output tiles on a cluster of two CTAs with tcgen05 cta_group::2:
+// CTA r of the pair loads rows [128r, 128r + 128) of the A tile, rows
+// [r*BN/2, (r+1)*BN/2) of the B tile, the scale atoms of its own A rows and
+// the scale atoms of all BN B rows; the even CTA issues one M=256 MMA per
+// 64-wide k-block for both.  Per SM this moves a third less operand data per
+// FLOP than a 128 x BN tile on one SM, and halves the MMA instructions.
+//
+// Synchronisation across the pair:
+//   full[s]      in CTA 0 only: both CTAs' TMA loads of stage s complete on it
+//                (cta_group::2 loads may signal the peer's barrier); CTA 0's
+//                producer posts the expected bytes of both.
+//   empty[s]     in both CTAs: CTA 0's commit arrives on both.
+//   acc_full[b]  in both CTAs: CTA 0's commit arrives on both.
+//   acc_empty[b] in CTA 0: the epilogue warps of both CTAs arrive (8 arrivals).
+//   mma_done     in both CTAs: the last commit; every MMA of the pair is done.
+// Scale-factor boxes are loaded with 3-D tensor maps over the atom array
+// ([row tile][k-block][512 bytes]) so they too can complete on CTA 0's barrier.
+//
+// 288 threads: warps 0-3 epilogue (warp w reads TMEM lanes 32w..32w+31),
+// warp 4 TMEM allocation and MMA issue, warps 5-8 one producer per copy type
+// (A, B, scale-A, scale-B).  A TMA issue keeps its warp busy for ~130 ns on
+// B200 and one thread's copies run one after another (~0.4 us each), so the
+// four copies of a stage go out from four warps in parallel, each from a lane
+// that has not issued for 32 stages.
+template <int BN, int STAGES>
+struct PairCfg {
+    static constexpr int kKbPerStage = 4;   // a stage covers K = 256: one 128-byte chunk
+    static_assert(BN % 64 == 0 && BN >= 128 && BN <= 256, "BN must be 128, 192 or 256");
+    static constexpr int BH = BN / 2;       // B rows held by each CTA
+    static constexpr int NRT = max_row_tiles(BN);
+    static constexpr int A_BYTES = kBM * kChunkBytes;
+    static constexpr int B_BYTES = BH * kChunkBytes;
+    static constexpr int SFA_BYTES = kKbPerStage * kAtomBytes;
+    static constexpr int SFB_BYTES = NRT * kKbPerStage * kAtomBytes;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+    // Every box is loaded whole (out-of-range parts read as zero), so a stage
+    // always brings the same bytes: those of both CTAs land on CTA 0's barrier.
+    static constexpr uint32_t TX_BYTES = 2u * STAGE_BYTES;
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    static constexpr int SF_COLS = 4 * kKbPerStage * (1 + NRT);
+    static constexpr int ACC_BUFS = (2 * BN + SF_COLS <= (int)kTmemCols) ? 2 : 1;
+    static constexpr uint32_t TMEM_SFA = ACC_BUFS * BN;
+    static constexpr uint32_t TMEM_SFB = TMEM_SFA + 4 * kKbPerStage;
+    static_assert(B_BYTES % 1024 == 0, "B stage must keep the 128B-swizzle alignment");
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
+    static_assert(TMEM_SFA + SF_COLS <= kTmemCols, "TMEM budget exceeded");
+};
+
+constexpr uint64_t kAbortDrainNs = 200000;  // after an abort, let issued copies land
+constexpr int kPairThreads = 288;
+constexpr int kPairMmaWarp = 4;
+constexpr int kPairFirstProducer = 5;
+
+template <int BN, int STAGES>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+    nvf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                          const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
+                          const __grid_constant__ Params p) {
+    using C = PairCfg<BN, STAGES>;
+    constexpr int kKbPerStage = C::kKbPerStage;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = sA + STAGES * C::A_BYTES;
+    uint8_t* sSFA = sB + STAGES * C::B_BYTES;
+    uint8_t* sSFB = sSFA + STAGES * C::SFA_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + STAGES * C::SFB_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* acc_full = empty + STAGES;     // [2]
+    uint64_t* acc_empty = acc_full + 2;      // [2]
+    uint64_t* mma_done = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = ptx::cluster_ctarank();  // 0: issues the pair's MMAs
+    const int pair = blockIdx.x >> 1;
+    const int npairs = gridDim.x >> 1;
+    const int num_kb = p.num_kb;
+    const int num_ks = (num_kb + kKbPerStage - 1) / kKbPerStage;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            ptx::mbar_init(&acc_full[b], 1);
+            ptx::mbar_init(&acc_empty[b], 2 * kEpilogueWarps);
+        }
+        ptx::mbar_init(mma_done, 1);
+        *s_abort = 0;
+        ptx::fence_mbar_init();
+        ptx::prefetch_tmap(&tmap_a);
+        ptx::prefetch_tmap(&tmap_b);
+        ptx::prefetch_tmap(&tmap_sfa);
+        ptx::prefetch_tmap(&tmap_sfb);
+    }
+    if (warp == kPairMmaWarp) {
+        ptx::tmem_alloc_pair(tmem_slot, kTmemCols);
+        ptx::tmem_relinquish_pair();
+    }
+    ptx::tc_fence_before();
+    // Both CTAs' barriers exist before any load, commit or arrive reaches them.
+    ptx::cluster_sync();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp >= kPairFirstProducer) {
+        // ------------------------------------------------------------ producers (both CTAs)
+        const int role = warp - kPairFirstProducer;  // 0 A, 1 B, 2 scale-A, 3 scale-B
+        const uint32_t full0 = ptx::map_to_cta(ptx::smem_u32(full), 0);
+        int it = 0;
+        bool stop = false;
+        for (int t = pair; t < p.num_tiles && !stop; t += npairs) {
+            const int m_tile = t / p.n_tiles;
+            const int n0 = (t - m_tile * p.n_tiles) * BN;
+            const int a_row = m_tile * 2 * kBM + (int)rank * kBM;
+            const int b_row = n0 + (int)rank * C::BH;
+            const int sfa_rt = m_tile * 2 + (int)rank;
+            const int sfb_rt = n0 >> 7;
+            for (int ks = 0; ks < num_ks; ++ks, ++it) {
+                const int s = it % STAGES;
+                if (it >= STAGES) {
+                    const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1));
+                    if (!ok) {
+                        if (lane == 0) {
+                            record_error(p.err, kErrProducerTimeout);
+                            atomicExch(s_abort, 1);
+                        }
+                        stop = true;
+                        break;
+                    }
+                }
+                if (__any_sync(0xffffffffu, aborted(s_abort))) {
+                    stop = true;
+                    break;
+                }
+                if (lane == (it & 31)) {
+                    const uint32_t bar = full0 + (uint32_t)s * 8u;
+                    const int kx = ks * kChunkBytes;
+                    const int kb0 = ks * kKbPerStage;
+                    if (role == 0) {
+                        if (rank == 0) ptx::mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
+                        ptx::tma_load_2d_pair(sA + s * C::A_BYTES, &tmap_a, bar, kx, a_row);
+                    } else if (role == 1) {
+                        ptx::tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_b, bar, kx, b_row);
+                    } else if (role == 2) {
+                        ptx::tma_load_3d_pair(sSFA + s * C::SFA_BYTES, &tmap_sfa, bar, 0, kb0, sfa_rt);
+                    } else {
+                        ptx::tma_load_3d_pair(sSFB + s * C::SFB_BYTES, &tmap_sfb, bar, 0, kb0, sfb_rt);
+                    }
+                }
+                __syncwarp();
+            }
+        }
+    } else if (warp == kPairMmaWarp) {
+        // ------------------------------------------------------------ MMA issuer (CTA 0)
+        if (rank == 0) {
+            const uint64_t adesc0 = ptx::desc_kmajor_sw128(ptx::smem_u32(sA));
+            const uint64_t bdesc0 = ptx::desc_kmajor_sw128(ptx::smem_u32(sB));
+            const uint64_t sfadesc0 = ptx::desc_sf_atom(ptx::smem_u32(sSFA));
+            const uint64_t sfbdesc0 = ptx::desc_sf_atom(ptx::smem_u32(sSFB));
+            constexpr uint32_t idesc = ptx::idesc_nvf4(BN, 2 * kBM);
+            int it = 0, tile_iter = 0;
+            bool stop = false;
+            for (int t = pair; t < p.num_tiles && !stop; t += npairs, ++tile_iter) {
+                const int n0 = (t % p.n_tiles) * BN;
+                const uint32_t shift_words = (n0 & 127) >> 5;
+                const int b = tile_iter % C::ACC_BUFS;
+                if (tile_iter >= C::ACC_BUFS) {
+                    const bool ok = __all_sync(0xffffffffu,
+                                               ptx::mbar_wait(&acc_empty[b], ((tile_iter / C::ACC_BUFS) & 1) ^ 1));
+                    if (!ok) {
+                        if (lane == 0) {
+                            record_error(p.err, kErrMmaTimeout);
+                            atomicExch(s_abort, 1);
+                        }
+                        break;
+                    }
+                }
+                ptx::tc_fence_after();
+                const uint32_t acc = tmem + b * BN;
+                const uint32_t sfa_t = tmem + C::TMEM_SFA;
+                const uint32_t sfb_t = tmem + C::TMEM_SFB;
+                for (int ks = 0; ks < num_ks; ++ks, ++it) {
+                    const int s = it % STAGES;
+                    const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(&full[s], (it / STAGES) & 1));
+                    if (!ok || __any_sync(0xffffffffu, aborted(s_abort))) {
+                        if (lane == 0) {
+                            record_error(p.err, kErrMmaTimeout);
+                            atomicExch(s_abort, 1);
+                        }
+                        stop = true;
+                        break;
+                    }
+                    ptx::tc_fence_after();
+                    const int nkb = min(kKbPerStage, num_kb - ks * kKbPerStage);
+                    const uint64_t a_s = adesc0 + (uint64_t)((s * C::A_BYTES) >> 4);
+                    const uint64_t b_s = bdesc0 + (uint64_t)((s * C::B_BYTES) >> 4);
+                    const uint64_t sfa_s = sfadesc0 + (uint64_t)((s * C::SFA_BYTES) >> 4);
+                    const uint64_t sfb_s = sfbdesc0 + (uint64_t)((s * C::SFB_BYTES) >> 4);
+                    const uint32_t first = (ks == 0) ? 0u : 1u;
+                    if (ptx::elect_one()) {
+#pragma unroll
+                        for (int j = 0; j < kKbPerStage; ++j) {
+                            if (j < nkb) {
+                                ptx::tc_cp_32x128b_warpx4_pair(sfa_t + 4 * j,
+                                                               sfa_s + (uint64_t)((j * kAtomBytes) >> 4));
+#pragma unroll
+                                for (int r = 0; r < C::NRT; ++r)
+                                    ptx::tc_cp_32x128b_warpx4_pair(
+                                        sfb_t + j * 4 * C::NRT + 4 * r,
+                                        sfb_s + (uint64_t)(((r * kKbPerStage + j) * kAtomBytes) >> 4));
+                            }
+                        }
+#pragma unroll
+                        for (int j = 0; j < kKbPerStage; ++j) {
+                            if (j < nkb) {
+                                const uint32_t koff = (uint32_t)((32 * j) >> 4);
+                                ptx::tc_mma_nvf4_pair(acc, a_s + koff, b_s + koff, idesc, sfa_t + 4 * j,
+                                                      sfb_t + j * 4 * C::NRT + shift_words, (j == 0) ? first : 1u);
+                            }
+                        }
+                        ptx::tc_commit_pair(&empty[s], 0x3);
+                    }
+                    __syncwarp();
+                }
+                if (!stop) {
+                    if (ptx::elect_one()) ptx::tc_commit_pair(&acc_full[b], 0x3);
+                    __syncwarp();
+                }
+            }
+            if (ptx::elect_one()) ptx::tc_commit_pair(mma_done, 0x3);
+            __syncwarp();
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        const int q = warp;
+        const uint32_t acc_empty0 = ptx::map_to_cta(ptx::smem_u32(acc_empty), 0);
+        int tile_iter = 0;
+        for (int t = pair; t < p.num_tiles; t += npairs, ++tile_iter) {
+            const int m_tile = t / p.n_tiles;
+            const int n0 = (t - m_tile * p.n_tiles) * BN;
+            const int m = m_tile * 2 * kBM + (int)rank * kBM + q * 32 + lane;
+            const int b = tile_iter % C::ACC_BUFS;
+            const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(&acc_full[b], (tile_iter / C::ACC_BUFS) & 1));
+            if (!ok || __any_sync(0xffffffffu, aborted(s_abort))) {
+                if (lane == 0 && !ok) {
+                    record_error(p.err, kErrEpilogueTimeout);
+                    atomicExch(s_abort, 1);
+                }
+                break;
+            }
+            ptx::tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + b * BN + 32 * c, r);
+                ptx::tmem_ld_wait();
+                if (c == BN / 32 - 1) {
+                    ptx::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive_cluster(acc_empty0 + (uint32_t)b * 8u);
+                }
+                if (m < p.m && n0 + 32 * c < p.n_out) store_chunk(p, r, m, n0 + 32 * c);
+            }
+        }
+    }
+
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // The last commit of CTA 0 reaches both CTAs once every MMA of the pair
+        // has completed (it reads both CTAs' shared memory and TMEM).
+        ptx::mbar_wait(mma_done, 0);
+        if (aborted(s_abort)) {
+            const uint64_t t0 = ptx::global_timer_ns();
+            while (ptx::global_timer_ns() - t0 < kAbortDrainNs) {
+            }
+        }
+    }
+    // Neither CTA leaves or frees TMEM while its peer may still signal it.
+    ptx::cluster_sync();
+    if (warp == kPairMmaWarp) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc_pair(tmem, kTmemCols);
+    }
+}
+
 // ------------------------------------------------------------------ host side
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -449,20 +744,23 @@ bool make_operand_map(CUtensorMap* map, const void* base, long rows, long k_pad,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES, int CHUNKS>
-cudaError_t launch_tile(const GemmArgs& g, cudaStream_t stream, int sms) {
-    using C = Cfg<BN, STAGES, CHUNKS>;
-    auto kernel = nvf4_gemm_kernel<BN, STAGES, CHUNKS>;
-    static std::once_flag attr_once[64];
-    int dev = 0;
-    cudaGetDevice(&dev);
-    std::call_once(attr_once[dev & 63], [&] {
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    });
-    CUtensorMap ma, mb;
-    if (!make_operand_map(&ma, g.a_fp4, g.m_rows_pad, g.k_pad, kBM) ||
-        !make_operand_map(&mb, g.b_fp4, g.n_rows_pad, g.k_pad, BN))
-        return cudaErrorInvalidValue;
+// Scale atoms of an operand with `rows_pad` rows as a 3-D array of 64-bit
+// words: [row tile][k-block][64 words = 512 bytes], boxes of kb_box k-blocks
+// x rt_box row tiles.  Boxes past the last k-block or row tile read zeros.
+bool make_scale_map(CUtensorMap* map, const void* base, long rows_pad, long k_pad, int kb_box, int rt_box) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const long num_kb = k_pad / 64;
+    const cuuint64_t dims[3] = {(cuuint64_t)(kAtomBytes / 8), (cuuint64_t)num_kb, (cuuint64_t)(rows_pad / 128)};
+    const cuuint64_t strides[2] = {(cuuint64_t)kAtomBytes, (cuuint64_t)(kAtomBytes * num_kb)};
+    const cuuint32_t box[3] = {(cuuint32_t)(kAtomBytes / 8), (cuuint32_t)kb_box, (cuuint32_t)rt_box};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+Params make_params(const GemmArgs& g, int bn, int tile_m) {
     Params p{};
     p.a_sf = g.a_sf;
     p.b_sf = g.b_sf;
@@ -481,8 +779,71 @@ cudaError_t launch_tile(const GemmArgs& g, cudaStream_t stream, int sms) {
     const bool d_al = (reinterpret_cast<uintptr_t>(g.d) & 15) == 0 && g.ldd % 8 == 0;
     const bool c_al = !g.c || ((reinterpret_cast<uintptr_t>(g.c) & 15) == 0 && g.ldc % 8 == 0);
     p.vec_store = (d_al && c_al) ? 1 : 0;
-    p.n_tiles = (int)((g.n_out + BN - 1) / BN);
-    p.num_tiles = p.n_tiles * (int)((g.m + kBM - 1) / kBM);
+    p.n_tiles = (int)((g.n_out + bn - 1) / bn);
+    p.num_tiles = p.n_tiles * (int)((g.m + tile_m - 1) / tile_m);
+    return p;
+}
+
+// Clusters of two resident at once for a pair kernel (one CTA per SM).
+template <typename K>
+int max_pairs(K kernel, int smem, int sms) {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int& c = cached[dev & 63];
+    if (c == 0) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+        cfg.blockDim = dim3(kPairThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, (const void*)kernel, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = sms / 2;
+        }
+        c = n;
+    }
+    return c;
+}
+
+template <int BN, int STAGES>
+cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms) {
+    using C = PairCfg<BN, STAGES>;
+    auto kernel = nvf4_gemm_pair_kernel<BN, STAGES>;
+    static std::once_flag attr_once[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::call_once(attr_once[dev & 63], [&] {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    });
+    CUtensorMap ma, mb, msa, msb;
+    if (!make_operand_map(&ma, g.a_fp4, g.m_rows_pad, g.k_pad, kBM) ||
+        !make_operand_map(&mb, g.b_fp4, g.n_rows_pad, g.k_pad, C::BH) ||
+        !make_scale_map(&msa, g.a_sf, g.m_rows_pad, g.k_pad, C::kKbPerStage, 1) ||
+        !make_scale_map(&msb, g.b_sf, g.n_rows_pad, g.k_pad, C::kKbPerStage, C::NRT))
+        return cudaErrorInvalidValue;
+    const Params p = make_params(g, BN, 2 * kBM);
+    const int pairs = max_pairs(kernel, C::SMEM_BYTES, sms);
+    const int grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);
+    kernel<<<grid, kPairThreads, C::SMEM_BYTES, stream>>>(ma, mb, msa, msb, p);
+    return cudaGetLastError();
+}
+
+template <int BN, int STAGES, int CHUNKS>
+cudaError_t launch_tile(const GemmArgs& g, cudaStream_t stream, int sms) {
+    using C = Cfg<BN, STAGES, CHUNKS>;
+    auto kernel = nvf4_gemm_kernel<BN, STAGES, CHUNKS>;
+    static std::once_flag attr_once[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::call_once(attr_once[dev & 63], [&] {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    });
+    CUtensorMap ma, mb;
+    if (!make_operand_map(&ma, g.a_fp4, g.m_rows_pad, g.k_pad, kBM) ||
+        !make_operand_map(&mb, g.b_fp4, g.n_rows_pad, g.k_pad, BN))
+        return cudaErrorInvalidValue;
+    const Params p = make_params(g, BN, kBM);
     const int grid = p.num_tiles < sms ? p.num_tiles : sms;
     kernel<<<grid, kThreads, C::SMEM_BYTES, stream>>>(ma, mb, p);
     return cudaGetLastError();
@@ -498,6 +859,24 @@ int choose_bn(long m, long n, int sms) {
         const long tiles = mt * ((n + bn - 1) / bn);
         const long waves = (tiles + sms - 1) / sms;
         const long cost = waves * bn;
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = bn;
+        }
+    }
+    return best;
+}
+
+// The same for 256-row tiles on sms/2 CTA pairs.
+int choose_bn_pair(long m, long n, int sms) {
+    static const int cands[] = {256, 192, 128};
+    const long mt = (m + 2 * kBM - 1) / (2 * kBM);
+    const long pairs = sms / 2 > 0 ? sms / 2 : 1;
+    int best = 128;
+    long best_cost = -1;
+    for (int bn : cands) {
+        const long tiles = mt * ((n + bn - 1) / bn);
+        const long cost = ((tiles + pairs - 1) / pairs) * bn;
         if (best_cost < 0 || cost < best_cost) {
             best_cost = cost;
             best = bn;
@@ -526,6 +905,20 @@ cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // CTA pairs (256-row tiles) once there are two 128-row tiles of A to
+    // share the B tile; FP4B_PAIR=0/1 forces the choice.
+    const char* pair_env = getenv("FP4B_PAIR");
+    const bool pair = pair_env ? atoi(pair_env) != 0 : g.m > kBM;
+    if (pair) {
+        const char* force = getenv("FP4B_FORCE_BN");
+        const int bn = force ? atoi(force) : choose_bn_pair(g.m, g.n_out, sms);
+        switch (bn) {
+            case 256: return launch_pair<256, 5>(g, stream, sms);
+            case 192: return launch_pair<192, 6>(g, stream, sms);
+            case 128: return launch_pair<128, 7>(g, stream, sms);
+            default: return cudaErrorInvalidValue;
+        }
+    }
     const char* force = getenv("FP4B_FORCE_BN");
     const int bn = force ? atoi(force) : choose_bn(g.m, g.n_out, sms);
     const char* stages_env = getenv("FP4B_DEEP");

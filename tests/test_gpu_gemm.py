@@ -2,8 +2,9 @@
 
 The reference GEMM (CUTLASS SM120, fp4_gemm_lib.cu:540-580) is pinned only by
 this tolerance: D must match alpha * dq(A) @ dq(B)^T + beta*C (+ bias) in fp32
-within max rel-err 1e-2 (tests/gpu_helpers.py).  Every tile width the kernel
-has is forced in turn; ragged M/N/K, K tails of half a stage, C/alpha/beta and
+within max rel-err 1e-2 (tests/gpu_helpers.py).  Both kernels (one CTA per
+128-row tile, and CTA pairs on 256-row tiles) are forced in turn with every
+tile width they have; ragged M/N/K, K tails of half a stage, C/alpha/beta and
 bias are covered, and the headline shape runs at full size.
 """
 import numpy as np
@@ -31,15 +32,17 @@ def run_prequant(fp4mod, x, w, bias=None, C=None, alpha=1.0, beta=0.0):
     return d
 
 
+@pytest.mark.parametrize("pair", [0, 1])
 @pytest.mark.parametrize("bn", TILES)
 @pytest.mark.parametrize("m,n,k", [(128, 256, 256), (256, 512, 1024), (200, 300, 384), (1, 8, 128),
                                    (384, 1000, 640)])
-def test_tile_widths(cuda, fp4, monkeypatch, bn, m, n, k):
+def test_tile_widths(cuda, fp4, monkeypatch, pair, bn, m, n, k):
     monkeypatch.setenv("FP4B_FORCE_BN", str(bn))
+    monkeypatch.setenv("FP4B_PAIR", str(pair))
     x = W.normal_bf16((m, k), 1.0, m + n)
     w = W.normal_bf16((n, k), 1.0, k)
     d = run_prequant(fp4, x, w)
-    assert_gemm_close(d, oracle_linear(x, w), f"bn={bn} {m}x{n}x{k}")
+    assert_gemm_close(d, oracle_linear(x, w), f"pair={pair} bn={bn} {m}x{n}x{k}")
     assert fp4.device_error() == 0
 
 
@@ -74,12 +77,25 @@ def test_headline_shape_full_size(cuda, fp4):
     assert abs(pearson(d.cpu(), exact) - pearson(ref, exact)) < 2e-4
 
 
-def test_accumulation_over_long_k(cuda, fp4):
-    # K = 16384 exercises many pipeline wraps of the smem ring.
-    x = W.normal_bf16((128, 16384), 1.0, 8)
+@pytest.mark.parametrize("m", [128, 512])
+def test_accumulation_over_long_k(cuda, fp4, m):
+    # K = 16384 exercises many pipeline wraps of the smem ring (m=512: CTA pairs).
+    x = W.normal_bf16((m, 16384), 1.0, 8)
     w = W.normal_bf16((256, 16384), 1.0, 9)
     d = run_prequant(fp4, x, w)
-    assert_gemm_close(d, oracle_linear(x, w), "K=16384")
+    assert_gemm_close(d, oracle_linear(x, w), f"{m}x256xK=16384")
+
+
+@pytest.mark.parametrize("pair", [0, 1])
+def test_many_tiles_per_cta(cuda, fp4, monkeypatch, pair):
+    # More tiles than SMs (pairs): every CTA walks several tiles, reusing
+    # both TMEM accumulators and the smem ring across tiles.
+    monkeypatch.setenv("FP4B_PAIR", str(pair))
+    m, n, k = 2304, 3200, 512
+    x = W.normal_bf16((m, k), 1.0, 21)
+    w = W.normal_bf16((n, k), 1.0, 22)
+    d = run_prequant(fp4, x, w)
+    assert_gemm_close(d, oracle_linear(x, w), f"pair={pair} {m}x{n}x{k}")
 
 
 def test_exact_small_integers(cuda, fp4):
