@@ -34,6 +34,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "fp4b_internal.h"
@@ -107,6 +108,8 @@ struct Params {
     long ldc, ldd;
     float alpha, beta;
     int vec_store;  // D/C rows 16-byte aligned
+    int tma_store;  // D written by TMA from shared memory (C unused, D rows 16-byte aligned)
+    int bias_vec;   // bias 16-byte aligned: read 8 values per load
 };
 
 // Error codes written to the device error word.
@@ -168,6 +171,78 @@ __device__ __forceinline__ void store_chunk(const Params& p, const uint32_t (&r)
         } else {
             for (int i = 0; i < 8 && n + i < p.n_out; ++i) drow[n + i] = __float2bfloat16_rn(v[i]);
         }
+    }
+}
+
+// Copies bias[n0, n0 + bn) into `dst` as fp32 (zeros past N) with the lanes
+// of one warp, so the epilogue reads it from shared memory.
+__device__ __forceinline__ void stage_bias(const Params& p, float4* dst, int n0, int bn, int lane) {
+    for (int i = lane; i < bn / 8; i += 32) {
+        const int nb = n0 + 8 * i;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (p.bias_vec && nb + 8 <= p.n_out) {
+            v = __ldg(reinterpret_cast<const uint4*>(p.bias + nb));
+        } else {
+            __nv_bfloat16* vb = reinterpret_cast<__nv_bfloat16*>(&v);
+            for (int j = 0; j < 8 && nb + j < p.n_out; ++j) vb[j] = p.bias[nb + j];
+        }
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+        const float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
+        const float2 f2 = __bfloat1622float2(h[2]), f3 = __bfloat1622float2(h[3]);
+        dst[2 * i] = make_float4(f0.x, f0.y, f1.x, f1.y);
+        dst[2 * i + 1] = make_float4(f2.x, f2.y, f3.x, f3.y);
+    }
+}
+
+// Epilogue of one 32 x 32 chunk through shared memory: thread t converts row
+// t (alpha*acc, BF16, optional BF16 bias) into a 2 KB buffer laid out in the
+// TMA 64-byte swizzle (16-byte unit u of row r at unit u ^ ((r >> 1) & 3),
+// which keeps the 16-byte shared stores of 8 consecutive rows on distinct
+// banks), then one lane stores the box [row0, row0 + 32) x [n, n + 32) with
+// TMA; rows past M and columns past N are clipped by the tensor map.
+// One thread's TMA copies run one after another (~0.4 us each), so chunk i
+// is stored by lane i % 32, and the lane that stored the buffer's previous
+// contents (chunk i - 1) waits until that store has read it.
+__device__ __forceinline__ void stage_chunk_tma(const Params& p, const CUtensorMap* tmap_d, const uint32_t (&r)[32],
+                                                const float4* sbias, uint8_t* buf, int row0, int n, int lane,
+                                                int chunk_iter) {
+    uint32_t packed[16];
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    if (p.alpha != 1.0f) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= p.alpha;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) packed[i] = bf16x2_bits(v[2 * i], v[2 * i + 1]);
+    if (p.bias) {
+        // Reference order: BF16 GEMM output, then a BF16 bias add (in fp32, rounded once).
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const float4 b = sbias[g];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t x = packed[2 * g + h];
+                const float lo = __uint_as_float(x << 16) + (h ? b.z : b.x);
+                const float hi = __uint_as_float(x & 0xFFFF0000u) + (h ? b.w : b.y);
+                packed[2 * g + h] = bf16x2_bits(lo, hi);
+            }
+        }
+    }
+    if (lane == ((chunk_iter - 1) & 31)) ptx::bulk_wait_group_read<0>();
+    __syncwarp();
+    uint8_t* row = buf + 64 * lane;
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(row + 16 * (u ^ sw)) =
+            make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == (chunk_iter & 31)) {
+        ptx::tma_store_2d(tmap_d, buf, n, row0);
+        ptx::bulk_commit_group();
     }
 }
 
@@ -439,12 +514,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Scale-factor boxes are loaded with 3-D tensor maps over the atom array
 // ([row tile][k-block][512 bytes]) so they too can complete on CTA 0's barrier.
 //
-// 288 threads: warps 0-3 epilogue (warp w reads TMEM lanes 32w..32w+31),
-// warp 4 TMEM allocation and MMA issue, warps 5-8 one producer per copy type
+// 416 threads: warps 0-7 epilogue (warp w reads TMEM lanes 32(w%4)..+31 and
+// stores the 32-column chunks c with c % 2 == w / 4), warp 8 TMEM allocation
+// and MMA issue, warps 9-12 one producer per copy type
 // (A, B, scale-A, scale-B).  A TMA issue keeps its warp busy for ~130 ns on
 // B200 and one thread's copies run one after another (~0.4 us each), so the
 // four copies of a stage go out from four warps in parallel, each from a lane
 // that has not issued for 32 stages.
+constexpr int kPairEpiWarps = 8;  // two per TMEM lane quadrant, each storing half of the columns
+
 template <int BN, int STAGES>
 struct PairCfg {
     static constexpr int kKbPerStage = 4;   // a stage covers K = 256: one 128-byte chunk
@@ -460,26 +538,30 @@ struct PairCfg {
     // always brings the same bytes: those of both CTAs land on CTA 0's barrier.
     static constexpr uint32_t TX_BYTES = 2u * STAGE_BYTES;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    // Epilogue staging: one 32 x 32 BF16 buffer (2 KB) and half the tile's bias per epilogue warp.
+    static constexpr int EPI_BYTES = kPairEpiWarps * 2048;          // one 32 x 32 BF16 buffer per epilogue warp
+    static constexpr int BIAS_BYTES = kPairEpiWarps * (BN / 2) * 4;  // fp32 bias of each warp's half of the tile
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + BIAS_BYTES + BAR_BYTES + 1024;
     static constexpr int SF_COLS = 4 * kKbPerStage * (1 + NRT);
     static constexpr int ACC_BUFS = (2 * BN + SF_COLS <= (int)kTmemCols) ? 2 : 1;
     static constexpr uint32_t TMEM_SFA = ACC_BUFS * BN;
     static constexpr uint32_t TMEM_SFB = TMEM_SFA + 4 * kKbPerStage;
     static_assert(B_BYTES % 1024 == 0, "B stage must keep the 128B-swizzle alignment");
+    static_assert(STAGE_BYTES % 1024 == 0, "epilogue buffers must stay 1024-byte aligned");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
     static_assert(TMEM_SFA + SF_COLS <= kTmemCols, "TMEM budget exceeded");
 };
 
 constexpr uint64_t kAbortDrainNs = 200000;  // after an abort, let issued copies land
-constexpr int kPairThreads = 288;
-constexpr int kPairMmaWarp = 4;
-constexpr int kPairFirstProducer = 5;
+constexpr int kPairThreads = 416;
+constexpr int kPairMmaWarp = 8;
+constexpr int kPairFirstProducer = 9;
 
 template <int BN, int STAGES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     nvf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-                          const __grid_constant__ Params p) {
+                          const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ Params p) {
     using C = PairCfg<BN, STAGES>;
     constexpr int kKbPerStage = C::kKbPerStage;
     extern __shared__ uint8_t smem_raw[];
@@ -488,7 +570,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     uint8_t* sB = sA + STAGES * C::A_BYTES;
     uint8_t* sSFA = sB + STAGES * C::B_BYTES;
     uint8_t* sSFB = sSFA + STAGES * C::SFA_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + STAGES * C::SFB_BYTES);
+    uint8_t* sEpi = sSFB + STAGES * C::SFB_BYTES;
+    float4* sBias = reinterpret_cast<float4*>(sEpi + C::EPI_BYTES);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + C::EPI_BYTES + C::BIAS_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;     // [2]
     uint64_t* acc_empty = acc_full + 2;      // [2]
@@ -511,7 +595,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             ptx::mbar_init(&acc_full[b], 1);
-            ptx::mbar_init(&acc_empty[b], 2 * kEpilogueWarps);
+            ptx::mbar_init(&acc_empty[b], 2 * kPairEpiWarps);
         }
         ptx::mbar_init(mma_done, 1);
         *s_abort = 0;
@@ -520,6 +604,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         ptx::prefetch_tmap(&tmap_b);
         ptx::prefetch_tmap(&tmap_sfa);
         ptx::prefetch_tmap(&tmap_sfb);
+        if (p.tma_store) ptx::prefetch_tmap(&tmap_d);
     }
     if (warp == kPairMmaWarp) {
         ptx::tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -661,14 +746,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         }
     } else {
         // ------------------------------------------------------------ epilogue (both CTAs)
-        const int q = warp;
+        const int q = warp & 3;   // TMEM lane quadrant
+        const int h = warp >> 2;  // chunks c = h, h + 2, ...
+        constexpr int kMyChunks = BN / 64;
         const uint32_t acc_empty0 = ptx::map_to_cta(ptx::smem_u32(acc_empty), 0);
+        uint8_t* epi = sEpi + warp * 2048;
+        float4* wbias = sBias + warp * (BN / 8);
+        int chunk_iter = 0;
         int tile_iter = 0;
         for (int t = pair; t < p.num_tiles; t += npairs, ++tile_iter) {
             const int m_tile = t / p.n_tiles;
             const int n0 = (t - m_tile * p.n_tiles) * BN;
             const int m = m_tile * 2 * kBM + (int)rank * kBM + q * 32 + lane;
             const int b = tile_iter % C::ACC_BUFS;
+            if (p.bias) {
+                __syncwarp();  // the previous tile's reads of wbias are done
+#pragma unroll
+                for (int j = 0; j < kMyChunks; ++j) stage_bias(p, wbias + 8 * j, n0 + 32 * (h + 2 * j), 32, lane);
+                __syncwarp();
+            }
             const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(&acc_full[b], (tile_iter / C::ACC_BUFS) & 1));
             if (!ok || __any_sync(0xffffffffu, aborted(s_abort))) {
                 if (lane == 0 && !ok) {
@@ -678,19 +774,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 break;
             }
             ptx::tc_fence_after();
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + b * BN + 32 * c, r);
+            // Only a later tile of this pair that reuses accumulator b waits for it.
+            const bool release = t + C::ACC_BUFS * npairs < p.num_tiles;
+            // The TMEM load of the next chunk is in flight while one is converted and stored.
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + b * BN + 32 * h;
+            uint32_t ra[32], rb[32];
+            ptx::tmem_ld_32x32b_x32(tbase, ra);
+#pragma unroll
+            for (int j = 0; j < kMyChunks; ++j) {
+                uint32_t(&r)[32] = (j & 1) ? rb : ra;
+                const int c = h + 2 * j;
                 ptx::tmem_ld_wait();
-                if (c == BN / 32 - 1) {
+                if (j + 1 < kMyChunks) {
+                    ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 1), (j & 1) ? ra : rb);
+                } else if (release) {
+                    // Every TMEM read of this accumulator is done: hand it back to the MMA issuer.
                     ptx::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) ptx::mbar_arrive_cluster(acc_empty0 + (uint32_t)b * 8u);
                 }
-                if (m < p.m && n0 + 32 * c < p.n_out) store_chunk(p, r, m, n0 + 32 * c);
+                if (n0 + 32 * c >= p.n_out) continue;
+                if (p.tma_store) {
+                    if (m - lane < p.m) {  // the warp's 32 rows start inside D
+                        stage_chunk_tma(p, &tmap_d, r, wbias + 8 * j, epi, m - lane, n0 + 32 * c, lane, chunk_iter);
+                        ++chunk_iter;
+                    }
+                } else if (m < p.m) {
+                    store_chunk(p, r, m, n0 + 32 * c);
+                }
             }
         }
+        ptx::bulk_wait_group_all();  // every lane's stores have read shared memory and written D
     }
 
     ptx::tc_fence_before();
@@ -760,6 +874,19 @@ bool make_scale_map(CUtensorMap* map, const void* base, long rows_pad, long k_pa
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// BF16 output D [m, n_out] with row stride ldd, 32 x 32 boxes, 64-byte swizzle.
+bool make_output_map(CUtensorMap* map, void* base, long m, long n_out, long ldd) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)n_out, (cuuint64_t)m};
+    const cuuint64_t strides[1] = {(cuuint64_t)(ldd * 2)};
+    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 Params make_params(const GemmArgs& g, int bn, int tile_m) {
     Params p{};
     p.a_sf = g.a_sf;
@@ -779,6 +906,8 @@ Params make_params(const GemmArgs& g, int bn, int tile_m) {
     const bool d_al = (reinterpret_cast<uintptr_t>(g.d) & 15) == 0 && g.ldd % 8 == 0;
     const bool c_al = !g.c || ((reinterpret_cast<uintptr_t>(g.c) & 15) == 0 && g.ldc % 8 == 0);
     p.vec_store = (d_al && c_al) ? 1 : 0;
+    p.bias_vec = (reinterpret_cast<uintptr_t>(g.bias) & 15) == 0 ? 1 : 0;
+    p.tma_store = 0;
     p.n_tiles = (int)((g.n_out + bn - 1) / bn);
     p.num_tiles = p.n_tiles * (int)((g.m + tile_m - 1) / tile_m);
     return p;
@@ -816,16 +945,21 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms) {
     std::call_once(attr_once[dev & 63], [&] {
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     });
-    CUtensorMap ma, mb, msa, msb;
+    CUtensorMap ma, mb, msa, msb, md;
     if (!make_operand_map(&ma, g.a_fp4, g.m_rows_pad, g.k_pad, kBM) ||
         !make_operand_map(&mb, g.b_fp4, g.n_rows_pad, g.k_pad, C::BH) ||
         !make_scale_map(&msa, g.a_sf, g.m_rows_pad, g.k_pad, C::kKbPerStage, 1) ||
         !make_scale_map(&msb, g.b_sf, g.n_rows_pad, g.k_pad, C::kKbPerStage, C::NRT))
         return cudaErrorInvalidValue;
-    const Params p = make_params(g, BN, 2 * kBM);
+    Params p = make_params(g, BN, 2 * kBM);
+    // D through TMA stores when C is not read and D's rows are 16-byte aligned.
+    memset(&md, 0, sizeof(md));
+    const bool no_c = !g.c || g.beta == 0.0f;
+    const bool d_ok = (reinterpret_cast<uintptr_t>(g.d) & 15) == 0 && g.ldd % 8 == 0;
+    if (no_c && d_ok && make_output_map(&md, g.d, g.m, g.n_out, g.ldd)) p.tma_store = 1;
     const int pairs = max_pairs(kernel, C::SMEM_BYTES, sms);
     const int grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);
-    kernel<<<grid, kPairThreads, C::SMEM_BYTES, stream>>>(ma, mb, msa, msb, p);
+    kernel<<<grid, kPairThreads, C::SMEM_BYTES, stream>>>(ma, mb, msa, msb, md, p);
     return cudaGetLastError();
 }
 
