@@ -92,6 +92,24 @@ FP4B_HD uint8_t e2m1_table_entry(uint32_t t) {
     return e2m1_scan(bits_f32((t + 1u) << 21));
 }
 
+// Bank-spread variant used by the GPU quantizer.  The kernel multiplies by
+// 32 / scale instead of 1 / scale (exact: a power-of-two factor on a product
+// that never underflows to zero for BF16 inputs), so the slots of |v| in
+// (2^-4, 8), i.e. of |v'| = 32|v| in (2, 256), are the bytes of the 4-byte
+// words 128..134 of the table: shared-memory banks 0..6.  The slot index of a
+// negative value has bit 6 flipped (banks 16..22), +0 and -0 land on banks 15
+// and 31, so the lookups of one warp do not conflict.  Entry i holds the code
+// of slot i ^ ((i >> 10) << 6) of 32v, i.e. of v at 1/32 of that slot's top.
+FP4B_HD uint32_t e2m1_banked_index(uint32_t bits_v32) {
+    const uint32_t t = bits_v32 - 1u;
+    return (t ^ ((t >> 4) & 0x08000000u)) >> 21;
+}
+
+FP4B_HD uint8_t e2m1_banked_entry(uint32_t i) {
+    const uint32_t t = i ^ ((i >> 10) << 6);
+    return e2m1_scan(bits_f32((t + 1u) << 21) * 0.03125f);
+}
+
 FP4B_HD uint8_t ue4m3_encode(float val) {
     val = fmax_ieee(val, kScaleMin);
     val = fmin_ieee(val, kScaleMax);
