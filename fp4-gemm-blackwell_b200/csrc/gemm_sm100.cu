@@ -301,6 +301,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Launched behind the activation quantizer: barriers and TMEM are set up
+    // while it finishes; no global memory is touched before this point.
+    ptx::grid_dependency_wait();
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -615,6 +618,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     ptx::cluster_sync();
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Launched behind the activation quantizer: barriers and TMEM are set up
+    // while it finishes; no global memory is touched before this point.
+    ptx::grid_dependency_wait();
 
     if (warp >= kPairFirstProducer) {
         // ------------------------------------------------------------ producers (both CTAs)
@@ -858,6 +864,24 @@ bool make_operand_map(CUtensorMap* map, const void* base, long rows, long k_pad,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Launch with programmatic stream serialization: the kernel may start while
+// the previous kernel on the stream finishes, and waits for it
+// (grid_dependency_wait) before touching global memory.
+template <typename K, typename... Args>
+cudaError_t launch_dependent(K kernel, dim3 grid, dim3 block, int smem, cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // Scale atoms of an operand with `rows_pad` rows as a 3-D array of 64-bit
 // words: [row tile][k-block][64 words = 512 bytes], boxes of kb_box k-blocks
 // x rt_box row tiles.  Boxes past the last k-block or row tile read zeros.
@@ -959,8 +983,7 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms) {
     if (no_c && d_ok && make_output_map(&md, g.d, g.m, g.n_out, g.ldd)) p.tma_store = 1;
     const int pairs = max_pairs(kernel, C::SMEM_BYTES, sms);
     const int grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);
-    kernel<<<grid, kPairThreads, C::SMEM_BYTES, stream>>>(ma, mb, msa, msb, md, p);
-    return cudaGetLastError();
+    return launch_dependent(kernel, dim3(grid), dim3(kPairThreads), C::SMEM_BYTES, stream, ma, mb, msa, msb, md, p);
 }
 
 template <int BN, int STAGES, int CHUNKS>
@@ -979,8 +1002,7 @@ cudaError_t launch_tile(const GemmArgs& g, cudaStream_t stream, int sms) {
         return cudaErrorInvalidValue;
     const Params p = make_params(g, BN, kBM);
     const int grid = p.num_tiles < sms ? p.num_tiles : sms;
-    kernel<<<grid, kThreads, C::SMEM_BYTES, stream>>>(ma, mb, p);
-    return cudaGetLastError();
+    return launch_dependent(kernel, dim3(grid), dim3(kThreads), C::SMEM_BYTES, stream, ma, mb, p);
 }
 
 // Pick the tile width that minimises (waves x BN) on this device.

@@ -178,6 +178,17 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         : "memory");
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Wait until the grid this one was launched behind (with programmatic stream
+// serialization) has completed and its memory writes are visible; returns at
+// once when there is none.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Let a grid launched behind this one start its prologue once every CTA of
+// this grid has issued this (it still waits for this grid to finish before
+// reading its results).
+__device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- TMA stores
 // Shared -> global tiled store (bulk-group completion); out-of-range parts of
 // the box are not written.

@@ -25,6 +25,7 @@
 
 #include "fp4b_internal.h"
 #include "nvfp4_codec.cuh"
+#include "ptx_sm100.cuh"
 
 namespace fp4b {
 
@@ -237,6 +238,9 @@ __global__ void __launch_bounds__(kThreads) nvfp4_quantize_kernel(const __grid_c
         if (threadIdx.x < 128) s_rcp32[threadIdx.x] = __ldg(&g_qtab.rcp32[threadIdx.x]);
     }
     __syncthreads();
+    // A GEMM launched behind this kernel may start setting up (it waits for
+    // this grid to complete before reading the quantized activations).
+    ptx::launch_dependents();
 
     for (;;) {
         quantize_and_store(p, base + threadIdx.x, end, w0, r0, kb0, lane, s_e2m1, s_sbyte, s_rcp32);
