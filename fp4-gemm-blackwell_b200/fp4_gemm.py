@@ -77,6 +77,16 @@ _bind("fp4b_weight_cache_import", _vp, [_vp, _vp, _i, _i, _vp])
 SF_VEC_SIZE = _lib.fp4_gemm_sf_vec_size()
 
 
+_SIDE_STREAMS = {}  # device -> (host-to-device, device-to-host) copy streams for forward_host
+
+
+def _chunk_schedule(m: int, chunk_rows: int) -> list:
+    """Row counts of forward_host's chunks.  Equal chunks of chunk_rows: on B200
+    with PCIe Gen5 a tail of halving chunks (512, 256, 128, ...) measured slower
+    than equal 512-row chunks, whose copies already hide the per-chunk GEMMs."""
+    return [min(chunk_rows, m - r) for r in range(0, m, chunk_rows)]
+
+
 def _pad_to_multiple(x: int, m: int) -> int:
     """Round up x to the nearest multiple of m."""
     return ((x + m - 1) // m) * m
@@ -348,6 +358,103 @@ class FP4WeightCache:
         D = D.reshape(*orig_shape[:-1], self.N_orig)
         return D
 
+    def forward_host(self, x: torch.Tensor, out: torch.Tensor = None, chunk_rows: int = 512) -> torch.Tensor:
+        """
+        Cached linear on host buffers: output = x @ cached_weight.T + bias with
+        x and the result in (pinned) CPU memory.
+
+        Rows are processed in chunks of ``chunk_rows`` (a multiple of 128):
+        the host-to-device copy of chunk c+1 runs on one side stream while
+        chunk c is quantized and multiplied on the caller's current stream and
+        chunk c-1 is copied back on another side stream, so the PCIe transfers
+        in both directions overlap each other and the GPU work; only the last
+        chunk's GEMM and copy back follow the last input copy.  The side streams
+        start after the work already queued on the current stream, and the
+        current stream waits for the last copy back, so the call is ordered
+        like any other stream operation; pass ``out`` (pinned, [..., N] BF16)
+        to reuse an output buffer, and synchronize before reading it.
+
+        Args:
+            x: Input activation [..., K] BF16 in CPU memory (pinned for overlap)
+            out: Optional CPU output [..., N] BF16
+            chunk_rows: rows per pipelined chunk
+
+        Returns:
+            CPU tensor [..., N] (``out`` when given)
+        """
+        if self._handle is None:
+            raise RuntimeError("FP4WeightCache has been freed")
+        if x.is_cuda:
+            raise ValueError("forward_host takes a CPU tensor; use forward for CUDA tensors")
+        if chunk_rows <= 0 or chunk_rows % 128:
+            raise ValueError("chunk_rows must be a positive multiple of 128")
+        orig_shape = x.shape
+        x_2d = x.reshape(-1, x.shape[-1])
+        if x_2d.shape[1] != self.K_orig:
+            raise ValueError(f"Input K={x_2d.shape[1]} doesn't match weight K={self.K_orig}")
+        if x_2d.dtype != torch.bfloat16:
+            x_2d = x_2d.to(torch.bfloat16)
+        x_2d = x_2d.contiguous()
+        M = x_2d.shape[0]
+        if out is None:
+            out = torch.empty(*orig_shape[:-1], self.N_orig, dtype=torch.bfloat16,
+                              pin_memory=torch.cuda.is_available())
+        if out.is_cuda or out.dtype != torch.bfloat16 or out.numel() != M * self.N_orig or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous CPU BF16 tensor of {M * self.N_orig} elements")
+        out_2d = out.view(M, self.N_orig)
+        if M == 0:
+            return out
+
+        dev = self.device
+        cur = torch.cuda.current_stream(dev)
+        h2d, d2h = self._side_streams()
+        xd, yd = self._host_staging(M)
+        bias = self.bias
+        fuse_bias = bias is not None and bias.dtype == torch.bfloat16 and bias.is_cuda
+        b_ptr = None
+        if fuse_bias:
+            bias = bias.reshape(-1).contiguous()
+            b_ptr = bias.data_ptr()
+        h2d.wait_stream(cur)
+        d2h.wait_stream(cur)
+        sptr = cur.cuda_stream
+        with torch.cuda.device(dev):
+            r1 = 0
+            for rows in _chunk_schedule(M, chunk_rows):
+                r0, r1 = r1, r1 + rows
+                with torch.cuda.stream(h2d):
+                    xd[r0:r1].copy_(x_2d[r0:r1], non_blocking=True)
+                cur.wait_stream(h2d)
+                rc = _lib.fp4b_run_cached_ex(xd[r0:r1].data_ptr(), r1 - r0, self.K_orig, self.K_orig, self._handle,
+                                             self.N_orig, None, 0, yd[r0:r1].data_ptr(), self.N_orig, b_ptr, 1.0,
+                                             0.0, sptr)
+                if rc != 0:
+                    raise RuntimeError(f"fp4_gemm_run_cached failed with error code {rc} ({_last_error()})")
+                if self.bias is not None and not fuse_bias:
+                    yd[r0:r1] += self.bias.to(device=dev, dtype=torch.bfloat16).unsqueeze(0)
+                d2h.wait_stream(cur)
+                with torch.cuda.stream(d2h):
+                    out_2d[r0:r1].copy_(yd[r0:r1], non_blocking=True)
+        cur.wait_stream(d2h)
+        return out
+
+    def _side_streams(self):
+        st = _SIDE_STREAMS.get(self.device)
+        if st is None:
+            st = (torch.cuda.Stream(self.device), torch.cuda.Stream(self.device))
+            _SIDE_STREAMS[self.device] = st
+        return st
+
+    def _host_staging(self, m: int):
+        """Device staging for forward_host: [m, K] input and [m, N] output, grow-only."""
+        st = getattr(self, "_staging", None)
+        if st is None or st[0].shape[0] < m:
+            rows = _pad_to_multiple(max(m, 128), 128)
+            st = (torch.empty(rows, self.K_orig, dtype=torch.bfloat16, device=self.device),
+                  torch.empty(rows, self.N_orig, dtype=torch.bfloat16, device=self.device))
+            self._staging = st
+        return st
+
     def shard(self, row0: int, rows: int, bias=None) -> "FP4WeightCache":
         """A cache viewing rows [row0, row0+rows) of this one (multiples of 128), for N-sharding."""
         h = _lib.fp4b_weight_cache_slice(self._handle, row0, rows)
@@ -392,9 +499,10 @@ class FP4WeightCache:
 
     def free(self):
         """Release GPU memory for cached weights."""
-        if getattr(self, "_handle", None):
+        if getattr(self, "_handle", None) and _lib is not None:
             _lib.fp4_weight_cache_free(ctypes.c_void_p(self._handle))
             self._handle = None
+        self._staging = None
 
     def __enter__(self):
         return self

@@ -182,3 +182,25 @@ def test_prealloc_and_cleanup(cuda, fp4):
         fp4._lib.fp4_gemm_cleanup()
         if fp4._lib.fp4_gemm_prealloc(0, 0, 0) != 0:
             raise RuntimeError("prealloc of an empty shape fails, as in the reference")
+
+
+@pytest.mark.parametrize("m,chunk", [(700, 256), (128, 128), (2048, 512)])
+def test_forward_host_equals_forward(cuda, fp4, m, chunk):
+    # Same kernels on the same rows: the pipelined host-buffer path must give
+    # the device path's bytes exactly, for ragged M and any chunking.
+    n, k = 640, 1024
+    x, w, b = W.cached_linear_inputs(m, n, k, seed=17)
+    with fp4.FP4WeightCache(w.to(cuda), b.to(cuda)) as cache:
+        want = cache.forward(x.to(cuda)).cpu()
+        got = cache.forward_host(x.pin_memory(), chunk_rows=chunk)
+        torch.cuda.synchronize()
+        assert not got.is_cuda and got.shape == (m, n)
+        assert torch.equal(got, want)
+        out = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+        assert cache.forward_host(x.reshape(1, m, k).pin_memory(), out=out.view(1, m, n)).data_ptr() == out.data_ptr()
+        torch.cuda.synchronize()
+        assert torch.equal(out, want)
+        with pytest.raises(ValueError):
+            cache.forward_host(x.to(cuda))
+        with pytest.raises(ValueError):
+            cache.forward_host(x, chunk_rows=100)
