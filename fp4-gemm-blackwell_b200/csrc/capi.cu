@@ -38,6 +38,7 @@ struct DeviceState {
     bool initialized = false;
     int M = 0, N = 0, K = 0;
     Buffer a_fp4, a_sf, b_fp4, b_sf;
+    Buffer sync;  // zeroed tile counters of the fused quantize+GEMM kernel
 };
 
 // g_mu guards the scratch state; launchers run while it is held, so anything
@@ -88,7 +89,22 @@ bool reserve(Buffer& b, size_t bytes) {
     return true;
 }
 
+// Grow-only buffer that is all zeros when handed out (the kernels using it
+// leave it zero).
+bool reserve_zeroed(Buffer& b, size_t bytes) {
+    if (b.cap >= bytes && b.ptr) return true;
+    if (!reserve(b, bytes)) return false;
+    if (cudaMemset(b.ptr, 0, b.cap) != cudaSuccess) {
+        cudaGetLastError();
+        release(b);
+        set_last_error("cudaMemset of the counter buffer failed");
+        return false;
+    }
+    return true;
+}
+
 void cleanup_state(DeviceState& s) {
+    release(s.sync);
     release(s.a_fp4);
     release(s.a_sf);
     release(s.b_fp4);
@@ -337,9 +353,16 @@ FP4B_EXPORT int fp4b_run_cached_ex(const void* A, int m, int k_in, int lda, cons
     DeviceState& s = g_state[current_device()];
     if (!reserve(s.a_fp4, (size_t)m_pad * c->K / 2) || !reserve(s.a_sf, (size_t)m_pad * c->K / 16)) return -1;
     cudaStream_t st = as_stream(stream);
-    if (int rc = quantize_into(A, m, k_in, lda, s.a_fp4.ptr, s.a_sf.ptr, m_pad, c->K, st)) return rc;
     GemmArgs g{s.a_fp4.ptr, s.a_sf.ptr, c->fp4, c->sf, m, n_out, c->K, m_pad, c->N, C, ldc, D, ldd, bias, alpha,
                beta};
+    QuantizeArgs q{A, m, k_in, lda, m_pad, c->K, s.a_fp4.ptr, s.a_sf.ptr};
+    if (m > 128 && !quantize_check(q) && !gemm_check(g) &&
+        reserve_zeroed(s.sync, (size_t)(1 + (m_pad + 255) / 256) * sizeof(uint32_t))) {
+        // One kernel quantizes the activations and multiplies (CTA-pair path).
+        const cudaError_t e = gemm_launch_fused(g, q, reinterpret_cast<uint32_t*>(s.sync.ptr), st);
+        if (e != cudaErrorNotSupported) return launch_status(e, "fused quantize+gemm launch");
+    }
+    if (int rc = quantize_into(A, m, k_in, lda, s.a_fp4.ptr, s.a_sf.ptr, m_pad, c->K, st)) return rc;
     return gemm_into(g, st);
 }
 

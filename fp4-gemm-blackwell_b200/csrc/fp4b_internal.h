@@ -43,6 +43,16 @@ struct GemmArgs {
 const char* gemm_check(const GemmArgs& g);
 cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream);
 
+// Cached linear with the activation quantization inside the GEMM kernel (the
+// CTA-pair path, M > 128; opt-in with FP4B_FUSE=1): the kernel quantizes `qa` (whose outputs must be
+// g.a_fp4 / g.a_sf) and multiplies.  `sync_words` is a device array of
+// 1 + ceil(m_rows_pad / 256) words that is zero before the first launch; the
+// kernel leaves it zero.  Launches that share `sync_words` must be ordered
+// (same stream).  Returns cudaErrorNotSupported when the fused path does not
+// apply; the caller then runs quantize_launch and gemm_launch.
+cudaError_t gemm_launch_fused(const GemmArgs& g, const QuantizeArgs& qa, uint32_t* sync_words,
+                              cudaStream_t stream);
+
 // Read-only view of a weight-cache handle created by the C ABI.
 struct CacheView {
     const uint8_t* fp4;

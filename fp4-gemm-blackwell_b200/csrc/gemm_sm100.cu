@@ -40,6 +40,7 @@
 #include "fp4b_internal.h"
 #include "nvfp4_codec.cuh"
 #include "ptx_sm100.cuh"
+#include "quantize_core.cuh"
 
 namespace fp4b {
 
@@ -110,12 +111,19 @@ struct Params {
     int vec_store;  // D/C rows 16-byte aligned
     int tma_store;  // D written by TMA from shared memory (C unused, D rows 16-byte aligned)
     int bias_vec;   // bias 16-byte aligned: read 8 values per load
+    // Fused activation quantization (pair kernel, FUSED): the kernel quantizes
+    // the BF16 activations described by `q` into a_fp4 / a_sf itself.
+    qcore::QuantParams q;
+    const qcore::QuantTables* qtab;
+    uint32_t* ready;  // [m_tiles] finished shares per 256-row tile, then one CTA-exit counter
+    int m_tiles;
 };
 
 // Error codes written to the device error word.
 constexpr int kErrProducerTimeout = 1;
 constexpr int kErrMmaTimeout = 2;
 constexpr int kErrEpilogueTimeout = 3;
+constexpr int kErrQuantizeWaitTimeout = 4;
 
 __device__ __forceinline__ void record_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
@@ -560,7 +568,88 @@ constexpr int kPairThreads = 416;
 constexpr int kPairMmaWarp = 8;
 constexpr int kPairFirstProducer = 9;
 
-template <int BN, int STAGES>
+// Fused mode: the epilogue warps of every CTA quantize an equal share of each
+// 256-row tile of A, tile by tile.  A warp takes every kWarps-th 32-block chunk
+// of its CTA's share, four chunks (one block per lane each) per group, and
+// issues the loads of its next group (of the same or a later tile) before
+// quantizing the current one.  Once a warp is past its last chunk of a tile
+// it adds one to ready[tile]; the A producers of that tile wait for
+// gridDim.x * kWarps.  The counters start at zero (the last CTA to exit
+// resets them).
+struct QuantGroup {
+    uint32_t w[4][8], r[4], kb[4], idx[4], end[4];
+};
+
+// Loads this warp's next group at or after chunk cursor (j, c); c = ~0 means
+// "first chunk of tile j".  Returns false when the warp has no chunks left;
+// on success j is the group's tile.
+template <int kWarps>
+__device__ __forceinline__ bool load_next_group(const Params& p, int warp, int lane, int& j, uint32_t& c,
+                                                QuantGroup& g) {
+    const qcore::QuantParams& q = p.q;
+    const uint32_t G = gridDim.x, per_tile = 256u * q.nsb;
+    for (; j < p.m_tiles; ++j, c = 0xFFFFFFFFu) {
+        const uint32_t b0 = (uint32_t)j * per_tile;
+        const uint32_t b1 = min(b0 + per_tile, q.total);
+        const uint32_t nch = (b1 - b0) >> 5;
+        const uint32_t c1 = (uint32_t)(((uint64_t)nch * (blockIdx.x + 1)) / G);
+        if (c == 0xFFFFFFFFu) c = (uint32_t)(((uint64_t)nch * blockIdx.x) / G) + (uint32_t)warp;
+        if (c < c1) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t ci = c + (uint32_t)(i * kWarps);
+                g.idx[i] = b0 + ci * 32u + (uint32_t)lane;
+                g.end[i] = ci < c1 ? b1 : 0u;
+                qcore::load_block(q, g.idx[i], g.end[i], g.w[i], g.r[i], g.kb[i]);
+            }
+            c += 4u * kWarps;
+            return true;
+        }
+    }
+    return false;
+}
+
+// Count tiles [counted, upto) as finished by this warp.
+__device__ __forceinline__ void count_tiles(const Params& p, int lane, int& counted, int upto) {
+    if (counted >= upto) return;
+    __syncwarp();  // every lane's stores of those tiles are issued
+    if (lane == 0) {
+        ptx::fence_proxy_async_global();
+        __threadfence();
+        for (int t = counted; t < upto; ++t) atomicAdd(p.ready + t, 1u);
+    }
+    counted = upto;
+}
+
+template <int kWarps>
+__device__ __forceinline__ void quantize_phase(const Params& p, const qcore::SmemTables& tab, int warp, int lane) {
+    int j = 0, counted = 0;
+    uint32_t c = 0xFFFFFFFFu;
+    QuantGroup cur, nxt;
+    bool have = load_next_group<kWarps>(p, warp, lane, j, c, cur);
+    int cur_tile = have ? j : p.m_tiles;
+    count_tiles(p, lane, counted, cur_tile);  // tiles before the first group hold nothing of this warp
+    while (have) {
+        int j2 = j;
+        uint32_t c2 = c;
+        const bool have2 = load_next_group<kWarps>(p, warp, lane, j2, c2, nxt);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            qcore::quantize_and_store(p.q, cur.idx[i], cur.end[i], cur.w[i], cur.r[i], cur.kb[i], (uint32_t)lane, tab);
+        const int next_tile = have2 ? j2 : p.m_tiles;
+        count_tiles(p, lane, counted, next_tile);  // tiles before the next group are done
+        have = have2;
+        if (have) {
+            cur = nxt;
+            cur_tile = j2;
+            j = j2;
+            c = c2;
+        }
+    }
+    count_tiles(p, lane, counted, p.m_tiles);
+}
+
+template <int BN, int STAGES, bool FUSED>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     nvf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
@@ -627,6 +716,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         const int role = warp - kPairFirstProducer;  // 0 A, 1 B, 2 scale-A, 3 scale-B
         const uint32_t full0 = ptx::map_to_cta(ptx::smem_u32(full), 0);
         int it = 0;
+        int ready_tile = -1;  // fused mode: last 256-row tile of A known to be quantized
         bool stop = false;
         for (int t = pair; t < p.num_tiles && !stop; t += npairs) {
             const int m_tile = t / p.n_tiles;
@@ -651,6 +741,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 if (__any_sync(0xffffffffu, aborted(s_abort))) {
                     stop = true;
                     break;
+                }
+                if constexpr (FUSED) {
+                    if ((role == 0 || role == 2) && m_tile != ready_tile) {
+                        // Every CTA's share of this tile of A is quantized and visible to TMA.
+                        bool ok = true;
+                        if (lane == 0) ok = ptx::wait_counter_geq(p.ready + m_tile, gridDim.x * kPairEpiWarps);
+                        ok = __shfl_sync(0xffffffffu, ok, 0);
+                        if (!ok) {
+                            if (lane == 0) {
+                                record_error(p.err, kErrQuantizeWaitTimeout);
+                                atomicExch(s_abort, 1);
+                            }
+                            stop = true;
+                            break;
+                        }
+                        ptx::fence_proxy_async_global();
+                        ready_tile = m_tile;
+                    }
                 }
                 if (lane == (it & 31)) {
                     const uint32_t bar = full0 + (uint32_t)s * 8u;
@@ -758,6 +866,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         const uint32_t acc_empty0 = ptx::map_to_cta(ptx::smem_u32(acc_empty), 0);
         uint8_t* epi = sEpi + warp * 2048;
         float4* wbias = sBias + warp * (BN / 8);
+        if constexpr (FUSED) {
+            // The quantizer tables live in the (not yet used) epilogue staging buffers.
+            static_assert(C::EPI_BYTES >= qcore::kSmemTableBytes, "tables must fit the staging buffers");
+            const qcore::SmemTables tab = qcore::copy_tables(p.qtab, sEpi, threadIdx.x, kPairEpiWarps * 32);
+            ptx::named_barrier(1, kPairEpiWarps * 32);
+            quantize_phase<kPairEpiWarps>(p, tab, warp, lane);
+            ptx::named_barrier(1, kPairEpiWarps * 32);  // tables no longer read: buffers free
+        }
         int chunk_iter = 0;
         int tile_iter = 0;
         for (int t = pair; t < p.num_tiles; t += npairs, ++tile_iter) {
@@ -822,6 +938,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         if (aborted(s_abort)) {
             const uint64_t t0 = ptx::global_timer_ns();
             while (ptx::global_timer_ns() - t0 < kAbortDrainNs) {
+            }
+        }
+    }
+    if constexpr (FUSED) {
+        // The last CTA to get here (all producers are past their waits) zeroes
+        // the tile counters for the next launch.
+        if (threadIdx.x == 0) {
+            __threadfence();
+            if (atomicAdd(p.ready + p.m_tiles, 1u) == gridDim.x - 1) {
+                for (int j = 0; j < p.m_tiles; ++j) atomicExch(p.ready + j, 0u);
+                atomicExch(p.ready + p.m_tiles, 0u);
+                __threadfence();
             }
         }
     }
@@ -959,10 +1087,11 @@ int max_pairs(K kernel, int smem, int sms) {
     return c;
 }
 
-template <int BN, int STAGES>
-cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms) {
+template <int BN, int STAGES, bool FUSED = false>
+cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const QuantizeArgs* qa = nullptr,
+                        uint32_t* sync_words = nullptr) {
     using C = PairCfg<BN, STAGES>;
-    auto kernel = nvf4_gemm_pair_kernel<BN, STAGES>;
+    auto kernel = nvf4_gemm_pair_kernel<BN, STAGES, FUSED>;
     static std::once_flag attr_once[64];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -981,6 +1110,13 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms) {
     const bool no_c = !g.c || g.beta == 0.0f;
     const bool d_ok = (reinterpret_cast<uintptr_t>(g.d) & 15) == 0 && g.ldd % 8 == 0;
     if (no_c && d_ok && make_output_map(&md, g.d, g.m, g.n_out, g.ldd)) p.tma_store = 1;
+    if constexpr (FUSED) {
+        p.qtab = quant_tables_device();
+        if (!p.qtab || !qa || !sync_words) return cudaErrorInvalidValue;
+        p.q = make_quant_params(*qa);
+        p.ready = sync_words;
+        p.m_tiles = (int)((g.m_rows_pad + 2 * kBM - 1) / (2 * kBM));
+    }
     const int pairs = max_pairs(kernel, C::SMEM_BYTES, sms);
     const int grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);
     return launch_dependent(kernel, dim3(grid), dim3(kPairThreads), C::SMEM_BYTES, stream, ma, mb, msa, msb, md, p);
@@ -1043,6 +1179,29 @@ int choose_bn_pair(long m, long n, int sms) {
 
 }  // namespace
 
+cudaError_t gemm_launch_fused(const GemmArgs& g, const QuantizeArgs& qa, uint32_t* sync_words,
+                              cudaStream_t stream) {
+    // Opt-in (FP4B_FUSE=1): with 8 quantizing warps per SM the quantize phase is
+    // latency-bound and delays the first tiles; on B200 the headline step took
+    // 60 us fused against 43 us for the quantize kernel followed by the GEMM.
+    const char* env = getenv("FP4B_FUSE");
+    if (!env || atoi(env) == 0 || g.m <= kBM || (getenv("FP4B_PAIR") && atoi(getenv("FP4B_PAIR")) == 0))
+        return cudaErrorNotSupported;
+    if (qa.rows_pad != g.m_rows_pad || qa.k_pad != g.k_pad || qa.fp4 != g.a_fp4 || qa.sf != g.a_sf)
+        return cudaErrorInvalidValue;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const char* force = getenv("FP4B_FORCE_BN");
+    const int bn = force ? atoi(force) : choose_bn_pair(g.m, g.n_out, sms);
+    switch (bn) {
+        case 256: return launch_pair<256, 5, true>(g, stream, sms, &qa, sync_words);
+        case 192: return launch_pair<192, 6, true>(g, stream, sms, &qa, sync_words);
+        case 128: return launch_pair<128, 7, true>(g, stream, sms, &qa, sync_words);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 const char* gemm_check(const GemmArgs& g) {
     if (!g.a_fp4 || !g.a_sf || !g.b_fp4 || !g.b_sf || !g.d) return "null pointer";
     if (g.m <= 0 || g.n_out <= 0) return "empty problem";
@@ -1069,9 +1228,9 @@ cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream) {
         const char* force = getenv("FP4B_FORCE_BN");
         const int bn = force ? atoi(force) : choose_bn_pair(g.m, g.n_out, sms);
         switch (bn) {
-            case 256: return launch_pair<256, 5>(g, stream, sms);
-            case 192: return launch_pair<192, 6>(g, stream, sms);
-            case 128: return launch_pair<128, 7>(g, stream, sms);
+            case 256: return launch_pair<256, 5, false>(g, stream, sms);
+            case 192: return launch_pair<192, 6, false>(g, stream, sms);
+            case 128: return launch_pair<128, 7, false>(g, stream, sms);
             default: return cudaErrorInvalidValue;
         }
     }

@@ -189,6 +189,29 @@ __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepco
 // reading its results).
 __device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// ---------------------------------------------------------------- cross-CTA counters
+// Bounded acquire spin until *ctr >= target; false after kSpinLimitNs.
+__device__ __forceinline__ bool wait_counter_geq(const uint32_t* ctr, uint32_t target) {
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+        if (v >= target) return true;
+        if (global_timer_ns() - t0 > kSpinLimitNs) return false;
+        __nanosleep(128);
+    }
+}
+
+// Order this thread's generic-proxy global accesses with its TMA (async proxy) ones.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Barrier over `nthreads` threads (whole warps) of the CTA on barrier `id` (1..15).
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ---------------------------------------------------------------- TMA stores
 // Shared -> global tiled store (bulk-group completion); out-of-range parts of
 // the box are not written.

@@ -1,0 +1,203 @@
+// quantize_core.cuh -- device code of the BF16 -> NVFP4 quantizer shared by
+// the standalone quantize kernel (quantize.cu) and the GEMM kernel that
+// quantizes its activations itself (gemm_sm100.cu).  The arithmetic is
+// described in quantize.cu.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "nvfp4_codec.cuh"
+
+namespace fp4b {
+namespace qcore {
+
+
+// |x|max (bf16 bits) below 6 * 2^-9 gives absmax/6 < 2^-9: the scale clamps to 0x01.
+constexpr uint32_t kScaleClampBf16 = 0x3C40u;
+constexpr int kScaleTableSize = (int)(kFastAbsmaxBf16Limit - kScaleClampBf16);  // 4672
+
+struct QuantTables {
+    uint8_t e2m1[kE2M1TableSize];    // code by bank-spread fp32 bit slot of 32v (e2m1_banked_entry)
+    uint8_t sbyte[kScaleTableSize];  // scale byte for |x|max bits kScaleClampBf16 + i
+    float rcp32[128];                // 32 * RN(1 / ue4m3_decode(byte)) (exact power-of-two factor)
+};
+static_assert(kScaleTableSize % 16 == 0, "tables are copied in 16-byte pieces");
+
+struct QuantParams {
+    const uint16_t* src;
+    uint8_t* fp4;
+    uint8_t* sf;
+    uint32_t rows, cols, ld;
+    uint32_t nsb;      // 16-element blocks per padded row
+    uint32_t total;    // rows_pad * nsb
+    uint32_t div_mul;  // fast division by nsb: q = (umulhi(n, div_mul) + n) >> div_shift
+    uint32_t div_shift;
+    uint32_t vec_ok;   // 16-byte aligned rows
+};
+
+// Shared-memory copies of the tables (copy_tables fills them).
+struct SmemTables {
+    const uint8_t* e2m1;
+    const uint8_t* sbyte;
+    const float* rcp32;
+};
+
+// Bytes of shared memory copy_tables needs (16-byte aligned start).
+constexpr int kSmemTableBytes = kE2M1TableSize + kScaleTableSize + 128 * 4;
+
+// Threads [0, nthreads) of the caller copy the tables from global memory into
+// `smem` (kSmemTableBytes, 16-byte aligned); the caller synchronizes after.
+__device__ __forceinline__ SmemTables copy_tables(const QuantTables* g, uint8_t* smem, int tid, int nthreads) {
+    const uint4* src = reinterpret_cast<const uint4*>(g);
+    uint4* dst = reinterpret_cast<uint4*>(smem);
+    static_assert(sizeof(QuantTables) == kSmemTableBytes, "table layout");
+    for (int i = tid; i < kSmemTableBytes / 16; i += nthreads) dst[i] = __ldg(src + i);
+    return SmemTables{smem, smem + kE2M1TableSize, reinterpret_cast<const float*>(smem + kE2M1TableSize + kScaleTableSize)};
+}
+
+// Round-up multiplier for exact unsigned division of n < 2^31 by d >= 1.
+inline void make_fast_div(uint32_t d, uint32_t* mul, uint32_t* shift) {
+    uint32_t s = 0;
+    while ((1ull << s) < d) ++s;
+    *shift = s;
+    *mul = (uint32_t)(((1ull << 32) * ((1ull << s) - d)) / d + 1);
+}
+
+// inv32 = 32 * RN(1 / scale): RN(x * inv32) = 32 * RN(x * RN(1 / scale)) whenever
+// the latter is a normal float; when it is not, |v| < 2^-126 and both give
+// code 0 with the same sign (no BF16 x underflows to zero here).
+__device__ __forceinline__ uint32_t e2m1_fast(float x, float inv32, const uint8_t* tab) {
+    return tab[e2m1_banked_index(__float_as_uint(__fmul_rn(x, inv32)))];
+}
+
+// Two packed BF16 -> byte of two E2M1 codes (low element in the low nibble).
+__device__ __forceinline__ uint32_t pack_pair_fast(uint32_t w, float inv32, const uint8_t* tab) {
+    const uint32_t lo = e2m1_fast(__uint_as_float(w << 16), inv32, tab);
+    const uint32_t hi = e2m1_fast(__uint_as_float(w & 0xFFFF0000u), inv32, tab);
+    return lo | (hi << 4);
+}
+
+// Element load with zero padding outside [rows, cols).
+__device__ __forceinline__ uint32_t load_pair(const uint16_t* src, uint32_t ld, uint32_t rows, uint32_t cols,
+                                              uint32_t r, uint32_t c) {
+    uint32_t lo = 0, hi = 0;
+    if (r < rows) {
+        const uint16_t* row = src + (size_t)r * ld;
+        if (c < cols) lo = row[c];
+        if (c + 1 < cols) hi = row[c + 1];
+    }
+    return lo | (hi << 16);
+}
+
+struct BlockOut {
+    uint32_t sbyte, out0, out1;
+};
+
+// Literal path for blocks holding NaN, Inf or |x| >= 2^30 (fp4_gemm_lib.cu:257-285).
+// Rare, so it reloads its 16 elements instead of keeping them live, and
+// returns its result by value (no stack traffic on the fast path).
+static __device__ __noinline__ BlockOut quantize_block_exact(const uint16_t* src, uint32_t ld, uint32_t rows,
+                                                      uint32_t cols, uint32_t r, uint32_t c0) {
+    float amax = 0.0f;
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t w = load_pair(src, ld, rows, cols, r, c0 + 2 * i);
+        amax = fmaxf(amax, fabsf(__uint_as_float(w << 16)));
+        amax = fmaxf(amax, fabsf(__uint_as_float(w & 0xFFFF0000u)));
+    }
+    float s = __fdiv_rn(amax, 6.0f);
+    if (s < kScaleMin) s = kScaleMin;
+    const uint8_t b = ue4m3_encode(s);
+    const float inv = __fdiv_rn(1.0f, ue4m3_decode(b));
+    uint32_t o0 = 0u, o1 = 0u;
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t w = load_pair(src, ld, rows, cols, r, c0 + 2 * i);
+        const uint32_t lo = e2m1_scan(__fmul_rn(__uint_as_float(w << 16), inv));
+        const uint32_t hi = e2m1_scan(__fmul_rn(__uint_as_float(w & 0xFFFF0000u), inv));
+        const uint32_t byte = (lo | (hi << 4)) << (8 * (i & 3));
+        if (i < 4) o0 |= byte; else o1 |= byte;
+    }
+    return BlockOut{b, o0, o1};
+}
+
+// Per half: max(|a|, |b|) as bf16 (a NaN operand gives NaN); the sign bit of
+// the result is not used.
+__device__ __forceinline__ uint32_t max_abs_bf16x2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+constexpr int kThreads = 256;
+constexpr int kBlocksPerThread = 2;  // 16-element blocks per thread per loop trip
+
+// Scale byte of a block from its |x|max (bf16 bits < kFastAbsmaxBf16Limit);
+// below 6 * 2^-9 the reference clamps the scale to 2^-9 (byte 0x01).
+__device__ __forceinline__ uint32_t scale_byte(uint32_t amax_bits, const uint8_t* s_sbyte) {
+    return amax_bits < kScaleClampBf16 ? 0x01u : (uint32_t)s_sbyte[amax_bits - kScaleClampBf16];
+}
+
+__device__ __forceinline__ void load_block(const QuantParams& p, uint32_t idx, uint32_t end, uint32_t (&w)[8],
+                                           uint32_t& r, uint32_t& kb) {
+    const bool valid = idx < end;
+    r = (__umulhi(idx, p.div_mul) + idx) >> p.div_shift;
+    kb = idx - r * p.nsb;
+    const uint32_t c0 = kb * kSfVec;
+    if (valid && p.vec_ok && r < p.rows && c0 + kSfVec <= p.cols) {
+        const uint4* g = reinterpret_cast<const uint4*>(p.src + (size_t)r * p.ld + c0);
+        const uint4 v0 = __ldcs(g);
+        const uint4 v1 = __ldcs(g + 1);
+        w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
+        w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
+    } else {
+        // Ragged edge, padding rows/columns or unaligned rows: element loads, zeros outside.
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[i] = valid ? load_pair(p.src, p.ld, p.rows, p.cols, r, c0 + 2 * i) : 0u;
+    }
+}
+
+__device__ __forceinline__ void quantize_and_store(const QuantParams& p, uint32_t idx, uint32_t end,
+                                                   const uint32_t (&w)[8],
+                                                   uint32_t r, uint32_t kb, uint32_t lane, const SmemTables& tab) {
+    const uint32_t m01 = max_abs_bf16x2(w[0], w[1]), m23 = max_abs_bf16x2(w[2], w[3]);
+    const uint32_t m45 = max_abs_bf16x2(w[4], w[5]), m67 = max_abs_bf16x2(w[6], w[7]);
+    const uint32_t mx = max_abs_bf16x2(max_abs_bf16x2(m01, m23), max_abs_bf16x2(m45, m67));
+    const uint32_t amax_bits = max(mx & 0x7FFFu, (mx >> 16) & 0x7FFFu);
+
+    uint32_t sbyte, out0 = 0, out1 = 0;
+    if (amax_bits < kFastAbsmaxBf16Limit) {
+        sbyte = scale_byte(amax_bits, tab.sbyte);
+        const float inv32 = tab.rcp32[sbyte];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            out0 |= pack_pair_fast(w[i], inv32, tab.e2m1) << (8 * i);
+            out1 |= pack_pair_fast(w[i + 4], inv32, tab.e2m1) << (8 * i);
+        }
+    } else {
+        const BlockOut o = quantize_block_exact(p.src, p.ld, p.rows, p.cols, r, kb * kSfVec);
+        sbyte = o.sbyte;
+        out0 = o.out0;
+        out1 = o.out1;
+    }
+    const bool valid = idx < end;
+    if (valid) *reinterpret_cast<uint2*>(p.fp4 + (size_t)idx * 8) = make_uint2(out0, out1);
+
+    // Scales of 4 consecutive blocks of one row are 4 consecutive bytes.
+    uint32_t sw = sbyte << (8 * (lane & 3u));
+    sw |= __shfl_xor_sync(0xffffffffu, sw, 1);
+    sw |= __shfl_xor_sync(0xffffffffu, sw, 2);
+    if (valid && (lane & 3u) == 0) *reinterpret_cast<uint32_t*>(p.sf + sf_offset(r, kb, p.nsb)) = sw;
+}
+
+
+}  // namespace qcore
+
+// Device address of the quantizer tables on the current device, uploaded on
+// first use (defined in quantize.cu).
+const qcore::QuantTables* quant_tables_device();
+
+struct QuantizeArgs;
+// Kernel parameters of a checked quantize call (defined in quantize.cu).
+qcore::QuantParams make_quant_params(const QuantizeArgs& a);
+
+}  // namespace fp4b

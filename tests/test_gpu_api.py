@@ -204,3 +204,22 @@ def test_forward_host_equals_forward(cuda, fp4, m, chunk):
             cache.forward_host(x.to(cuda))
         with pytest.raises(ValueError):
             cache.forward_host(x, chunk_rows=100)
+
+
+@pytest.mark.parametrize("m,n,k", [(2048, 2880, 7680), (200, 300, 384), (384, 1000, 640), (4096, 640, 1024)])
+def test_fused_quantize_gemm_equals_two_kernels(cuda, fp4, monkeypatch, m, n, k):
+    # With FP4B_FUSE=1 and M > 128 the cached linear quantizes the activations
+    # inside the GEMM kernel; the result must be the two-kernel path's bytes
+    # exactly.
+    x, w, b = W.cached_linear_inputs(m, n, k, seed=23)
+    with fp4.FP4WeightCache(w.to(cuda), b.to(cuda)) as cache:
+        xd = x.to(cuda)
+        monkeypatch.setenv("FP4B_FUSE", "0")
+        two = cache.forward(xd)
+        monkeypatch.setenv("FP4B_FUSE", "1")
+        fused = [cache.forward(xd) for _ in range(3)]  # repeated launches reuse the tile counters
+        torch.cuda.synchronize()
+        for f in fused:
+            assert torch.equal(f, two)
+        assert fp4.device_error() == 0
+    assert_gemm_close(two, oracle_linear(x, w, bias=b), f"fused {m}x{n}x{k}")
