@@ -106,6 +106,7 @@ struct Params {
     int m, n_out, num_kb;  // num_kb = k_pad / 64
     int n_rows_pad;
     int n_tiles, num_tiles;
+    int m_tiles;  // row tiles of the output (128 rows, or 256 for CTA pairs)
     long ldc, ldd;
     float alpha, beta;
     int vec_store;  // D/C rows 16-byte aligned
@@ -116,8 +117,24 @@ struct Params {
     qcore::QuantParams q;
     const qcore::QuantTables* qtab;
     uint32_t* ready;  // [m_tiles] finished shares per 256-row tile, then one CTA-exit counter
-    int m_tiles;
 };
+
+// Tile t -> (row tile, column tile) in groups of kTileGroupRows rows of A: the
+// tiles in flight at one time cover a few row tiles and a few column tiles,
+// so the A and B tiles they read stay in L2 even when B is larger than L2
+// (the group's row tiles are revisited for every column tile of B).
+constexpr int kTileGroupRows = 2048;
+
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int tile_m, int& m_tile, int& n_tile) {
+    const int group = kTileGroupRows / tile_m;
+    const int per_group = group * n_tiles;
+    const int g = t / per_group;
+    const int first_m = g * group;
+    const int gm = min(group, m_tiles - first_m);
+    const int local = t - g * per_group;
+    m_tile = first_m + local % gm;
+    n_tile = local / gm;
+}
 
 // Error codes written to the device error word.
 constexpr int kErrProducerTimeout = 1;
@@ -262,6 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     nvf4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                      const __grid_constant__ Params p) {
     using C = Cfg<BN, STAGES, CHUNKS>;
+    constexpr int TILE_M = kBM;
     constexpr int kChunks = C::kChunks;
     constexpr int kStageKBytes = C::kStageKBytes;
     constexpr int kKbPerStage = C::kKbPerStage;
@@ -321,8 +339,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         int it = 0;
         bool stop = false;
         for (int t = blockIdx.x; t < p.num_tiles && !stop; t += gridDim.x) {
-            const int m_tile = t / p.n_tiles;
-            const int n0 = (t - m_tile * p.n_tiles) * BN;
+            int m_tile, n_tile;
+            tile_coords(t, p.m_tiles, p.n_tiles, TILE_M, m_tile, n_tile);
+            const int n0 = n_tile * BN;
             const int m0 = m_tile * kBM;
             const int rt0 = n0 >> 7;
             int nrt = ((n0 & 127) + BN + 127) >> 7;
@@ -381,7 +400,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         int it = 0, tile_iter = 0;
         bool stop = false;
         for (int t = blockIdx.x; t < p.num_tiles && !stop; t += gridDim.x, ++tile_iter) {
-            const int n0 = (t % p.n_tiles) * BN;
+            int m_tile_unused, n_tile;
+            tile_coords(t, p.m_tiles, p.n_tiles, TILE_M, m_tile_unused, n_tile);
+            const int n0 = n_tile * BN;
             int nrt = ((n0 & 127) + BN + 127) >> 7;
             if ((n0 >> 7) + nrt > (p.n_rows_pad >> 7)) nrt = (p.n_rows_pad >> 7) - (n0 >> 7);
             const uint32_t shift_words = (n0 & 127) >> 5;
@@ -458,8 +479,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp & 3;  // TMEM lane quadrant this warp may read
         int tile_iter = 0;
         for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++tile_iter) {
-            const int m_tile = t / p.n_tiles;
-            const int n0 = (t - m_tile * p.n_tiles) * BN;
+            int m_tile, n_tile;
+            tile_coords(t, p.m_tiles, p.n_tiles, TILE_M, m_tile, n_tile);
+            const int n0 = n_tile * BN;
             const int m = m_tile * kBM + q * 32 + lane;
             const int b = tile_iter % C::ACC_BUFS;
             const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(&acc_full[b], (tile_iter / C::ACC_BUFS) & 1));
@@ -655,6 +677,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
                           const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ Params p) {
     using C = PairCfg<BN, STAGES>;
+    constexpr int TILE_M = 2 * kBM;
     constexpr int kKbPerStage = C::kKbPerStage;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -719,8 +742,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         int ready_tile = -1;  // fused mode: last 256-row tile of A known to be quantized
         bool stop = false;
         for (int t = pair; t < p.num_tiles && !stop; t += npairs) {
-            const int m_tile = t / p.n_tiles;
-            const int n0 = (t - m_tile * p.n_tiles) * BN;
+            int m_tile, n_tile;
+            tile_coords(t, p.m_tiles, p.n_tiles, TILE_M, m_tile, n_tile);
+            const int n0 = n_tile * BN;
             const int a_row = m_tile * 2 * kBM + (int)rank * kBM;
             const int b_row = n0 + (int)rank * C::BH;
             const int sfa_rt = m_tile * 2 + (int)rank;
@@ -789,7 +813,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             int it = 0, tile_iter = 0;
             bool stop = false;
             for (int t = pair; t < p.num_tiles && !stop; t += npairs, ++tile_iter) {
-                const int n0 = (t % p.n_tiles) * BN;
+                int m_tile_unused, n_tile;
+                tile_coords(t, p.m_tiles, p.n_tiles, TILE_M, m_tile_unused, n_tile);
+                const int n0 = n_tile * BN;
                 const uint32_t shift_words = (n0 & 127) >> 5;
                 const int b = tile_iter % C::ACC_BUFS;
                 if (tile_iter >= C::ACC_BUFS) {
@@ -877,8 +903,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         int chunk_iter = 0;
         int tile_iter = 0;
         for (int t = pair; t < p.num_tiles; t += npairs, ++tile_iter) {
-            const int m_tile = t / p.n_tiles;
-            const int n0 = (t - m_tile * p.n_tiles) * BN;
+            int m_tile, n_tile;
+            tile_coords(t, p.m_tiles, p.n_tiles, TILE_M, m_tile, n_tile);
+            const int n0 = n_tile * BN;
             const int m = m_tile * 2 * kBM + (int)rank * kBM + q * 32 + lane;
             const int b = tile_iter % C::ACC_BUFS;
             if (p.bias) {
@@ -1061,7 +1088,8 @@ Params make_params(const GemmArgs& g, int bn, int tile_m) {
     p.bias_vec = (reinterpret_cast<uintptr_t>(g.bias) & 15) == 0 ? 1 : 0;
     p.tma_store = 0;
     p.n_tiles = (int)((g.n_out + bn - 1) / bn);
-    p.num_tiles = p.n_tiles * (int)((g.m + tile_m - 1) / tile_m);
+    p.m_tiles = (int)((g.m + tile_m - 1) / tile_m);
+    p.num_tiles = p.n_tiles * p.m_tiles;
     return p;
 }
 
@@ -1115,7 +1143,6 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const Q
         if (!p.qtab || !qa || !sync_words) return cudaErrorInvalidValue;
         p.q = make_quant_params(*qa);
         p.ready = sync_words;
-        p.m_tiles = (int)((g.m_rows_pad + 2 * kBM - 1) / (2 * kBM));
     }
     const int pairs = max_pairs(kernel, C::SMEM_BYTES, sms);
     const int grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);

@@ -63,3 +63,26 @@ def pearson(a: torch.Tensor, b: torch.Tensor) -> float:
     a = a - a.mean()
     b = b - b.mean()
     return float((a @ b) / (a.norm() * b.norm()))
+
+
+_E2M1 = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]
+
+
+def dequant_torch(fp4: torch.Tensor, sf: torch.Tensor, rows_pad: int, k_pad: int) -> torch.Tensor:
+    """fp32 [rows_pad, k_pad] from packed E2M1 bytes and 128x4-atom UE4M3 scales,
+    on the tensors' device (a torch restatement of oracle.dequantize for sizes
+    the CPU oracle cannot finish quickly)."""
+    dev = fp4.device
+    lut = torch.tensor(_E2M1, dtype=torch.float32, device=dev)
+    b = fp4.reshape(rows_pad, k_pad // 2).to(torch.int64)
+    vals = torch.stack([lut[b & 0xF], lut[b >> 4]], dim=-1).reshape(rows_pad, k_pad)
+    # UE4M3 decode of all 256 byte values: (8 + m) * 2^(e - 10), subnormal m * 2^-9
+    codes = torch.arange(256, device=dev)
+    e, m = (codes >> 3) & 0xF, (codes & 7).to(torch.float32)
+    dec = torch.where(e == 0, m * 2.0 ** -9, (8 + m) * torch.pow(2.0, (e - 10).to(torch.float32)))
+    nsb = k_pad // 16
+    r = torch.arange(rows_pad, device=dev).unsqueeze(1)
+    kb = torch.arange(nsb, device=dev).unsqueeze(0)
+    off = (r % 32) * 16 + ((r // 32) % 4) * 4 + (kb % 4) + (kb // 4) * 512 + (r // 128) * 512 * (nsb // 4)
+    scale = dec[sf.reshape(-1).to(torch.int64)[off]]  # [rows_pad, nsb]
+    return vals * scale.repeat_interleave(16, dim=1)

@@ -113,3 +113,40 @@ def test_exact_small_integers(cuda, fp4):
     assert torch.equal(d.float().cpu(), ref.to(torch.bfloat16).float())
     aq, asf = oracle_quantize(x)
     assert torch.equal(oracle_dequant(aq, asf, 128, 256), x.float())
+
+
+def test_dynamic_8192_cubed_against_torch_fp32(cuda, fp4):
+    # Config 3 at full size: both operands quantized on the GPU (bytes pinned
+    # elsewhere against the oracle), the GEMM checked against torch fp32 (no
+    # TF32) on the dequantized operands.
+    from tests.gpu_helpers import dequant_torch
+    n = 8192
+    g = torch.Generator(device=cuda).manual_seed(5)
+    a = torch.randn(n, n, generator=g, device=cuda).to(torch.bfloat16)
+    b = torch.randn(n, n, generator=g, device=cuda).to(torch.bfloat16)
+    aq, asf = fp4.quantize_to_buffers(a, None, n)
+    bq, bsf = fp4.quantize_to_buffers(b, None, n)
+    d = fp4.gemm_prequantized(aq, asf, n, bq, bsf, n, n)
+    torch.cuda.synchronize()
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref = dequant_torch(aq, asf, n, n) @ dequant_torch(bq, bsf, n, n).t()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    err = (d.float() - ref).abs()
+    scale = ref.abs().max()
+    assert err.max() <= 1e-2 * scale, (err.max().item(), scale.item())
+    assert not (err > 1e-2 * ref.abs() + 1e-3 * scale).any()
+    # and the dynamic API gives the same bytes
+    assert torch.equal(fp4.fp4_matmul(a, b), d)
+
+
+def test_dequant_torch_matches_oracle(cuda, fp4):
+    from tests.gpu_helpers import dequant_torch, oracle_dequant
+    x = W.normal_bf16((256, 384), 1.0, 31)
+    aq, asf = fp4.quantize_to_buffers(x.to(cuda), None, 384)
+    torch.cuda.synchronize()
+    got = dequant_torch(aq, asf, 256, 384).cpu()
+    want = oracle_dequant(aq.cpu().numpy().reshape(-1), asf.cpu().numpy().reshape(-1), 256, 384)
+    assert torch.equal(got, want)
