@@ -6,6 +6,7 @@
 // underneath: the reference's single global FP4GemmState becomes one scratch
 // state per CUDA device behind a mutex, every allocation is checked, and the
 // kernels are the sm_100a ones in quantize.cu / gemm_sm100.cu.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -364,6 +365,101 @@ FP4B_EXPORT int fp4b_run_cached_ex(const void* A, int m, int k_in, int lda, cons
     }
     if (int rc = quantize_into(A, m, k_in, lda, s.a_fp4.ptr, s.a_sf.ptr, m_pad, c->K, st)) return rc;
     return gemm_into(g, st);
+}
+
+FP4B_EXPORT int fp4b_run_cached_peers(const void* A, int m, int k_in, int lda, const void* h, int n_out,
+                                      void* D, int ldd, void* const* peer_d, int npeers, const void* bias,
+                                      void* stream) {
+    WeightCache* c = as_cache(h);
+    if (!c) {
+        set_last_error("null or invalid cache handle");
+        return -1;
+    }
+    if (!A || !D || m <= 128 || k_in <= 0 || k_in > c->K || lda < k_in || n_out <= 0 || n_out > c->N ||
+        !peer_d || npeers < 1 || npeers > 7) {
+        set_last_error("fp4b_run_cached_peers: bad arguments (m=%d must exceed 128, 1..7 peers)", m);
+        return -1;
+    }
+    const long m_pad = round_up(m, 128);
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceState& s = g_state[current_device()];
+    if (!reserve(s.a_fp4, (size_t)m_pad * c->K / 2) || !reserve(s.a_sf, (size_t)m_pad * c->K / 16)) return -1;
+    cudaStream_t st = as_stream(stream);
+    GemmArgs g{s.a_fp4.ptr, s.a_sf.ptr, c->fp4, c->sf, m, n_out, c->K, m_pad, c->N, nullptr, 0, D, ldd, bias, 1.0f,
+               0.0f};
+    if (const char* why = gemm_check(g)) {
+        set_last_error("gemm: %s", why);
+        return -2;
+    }
+    if (int rc = quantize_into(A, m, k_in, lda, s.a_fp4.ptr, s.a_sf.ptr, m_pad, c->K, st)) return rc;
+    const cudaError_t e = gemm_launch_peers(g, peer_d, npeers, st);
+    if (e == cudaErrorNotSupported) {
+        set_last_error("fp4b_run_cached_peers: needs 16-byte aligned output rows");
+        return -2;
+    }
+    return launch_status(e, "peer gemm launch");
+}
+
+namespace {
+using GetAddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+GetAddressRangeFn address_range_fn() {
+    static GetAddressRangeFn fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<GetAddressRangeFn>(f);
+    }();
+    return fn;
+}
+}  // namespace
+
+FP4B_EXPORT int fp4b_ipc_get_handle(const void* ptr, void* handle_out, long* offset_out) {
+    GetAddressRangeFn range = address_range_fn();
+    if (!ptr || !handle_out || !offset_out || !range) {
+        set_last_error("fp4b_ipc_get_handle: bad arguments or no driver entry point");
+        return -1;
+    }
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) {
+        set_last_error("fp4b_ipc_get_handle: pointer is not device memory");
+        return -1;
+    }
+    cudaIpcMemHandle_t hdl;
+    if (cudaIpcGetMemHandle(&hdl, reinterpret_cast<void*>(base)) != cudaSuccess) {
+        cudaGetLastError();
+        set_last_error("cudaIpcGetMemHandle failed");
+        return -1;
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    memcpy(handle_out, &hdl, sizeof(hdl));
+    *offset_out = (long)(reinterpret_cast<CUdeviceptr>(ptr) - base);
+    return 0;
+}
+
+FP4B_EXPORT void* fp4b_ipc_open_handle(const void* handle, long offset) {
+    if (!handle || offset < 0) return nullptr;
+    cudaIpcMemHandle_t hdl;
+    memcpy(&hdl, handle, sizeof(hdl));
+    void* base = nullptr;
+    if (cudaIpcOpenMemHandle(&base, hdl, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        set_last_error("cudaIpcOpenMemHandle failed");
+        return nullptr;
+    }
+    return static_cast<uint8_t*>(base) + offset;
+}
+
+FP4B_EXPORT int fp4b_ipc_close(void* ptr, long offset) {
+    if (!ptr) return -1;
+    if (cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset) != cudaSuccess) {
+        cudaGetLastError();
+        set_last_error("cudaIpcCloseMemHandle failed");
+        return -1;
+    }
+    return 0;
 }
 
 FP4B_EXPORT int fp4_gemm_run_cached(const void* A, const void* h, const void* C, void* D, int M, float alpha,

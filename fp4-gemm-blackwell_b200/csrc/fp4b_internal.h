@@ -50,6 +50,13 @@ cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream);
 // kernel leaves it zero.  Launches that share `sync_words` must be ordered
 // (same stream).  Returns cudaErrorNotSupported when the fused path does not
 // apply; the caller then runs quantize_launch and gemm_launch.
+// GEMM whose output tile is also stored into `npeers` (1..7) other BF16
+// buffers with the same row stride (other GPUs' memory mapped into this
+// process, each offset to the columns this rank computes): the column-parallel
+// all-gather done by the epilogue.  CTA-pair path only (M > 128), no C, D rows
+// 16-byte aligned; else cudaErrorNotSupported.
+cudaError_t gemm_launch_peers(const GemmArgs& g, void* const* peers, int npeers, cudaStream_t stream);
+
 cudaError_t gemm_launch_fused(const GemmArgs& g, const QuantizeArgs& qa, uint32_t* sync_words,
                               cudaStream_t stream);
 

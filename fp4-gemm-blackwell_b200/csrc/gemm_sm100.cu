@@ -96,6 +96,8 @@ struct Cfg {
     static_assert(TMEM_SFA + SF_COLS <= kTmemCols, "TMEM budget exceeded");
 };
 
+constexpr int kMaxPeers = 7;
+
 struct Params {
     const uint8_t* a_sf;
     const uint8_t* b_sf;
@@ -117,6 +119,11 @@ struct Params {
     qcore::QuantParams q;
     const qcore::QuantTables* qtab;
     uint32_t* ready;  // [m_tiles] finished shares per 256-row tile, then one CTA-exit counter
+    // Column-parallel output (pair kernel, TMA-store epilogue): every tile is
+    // also written to npeers other [m, ldd] BF16 buffers (other GPUs' memory
+    // mapped into this process), each already offset to this rank's columns.
+    __nv_bfloat16* peer_d[kMaxPeers];
+    int npeers;
 };
 
 // Tile t -> (row tile, column tile) in groups of kTileGroupRows rows of A: the
@@ -268,6 +275,26 @@ __device__ __forceinline__ void stage_chunk_tma(const Params& p, const CUtensorM
     if (lane == (chunk_iter & 31)) {
         ptx::tma_store_2d(tmap_d, buf, n, row0);
         ptx::bulk_commit_group();
+    }
+    if (p.npeers > 0) {
+        // Peer copies over NVLink with plain 16-byte stores: the staged chunk is
+        // read back row by row, four lanes per 64-byte row segment.
+#pragma unroll
+        for (int pass = 0; pass < 4; ++pass) {
+            const int rr = pass * 8 + (lane >> 2), u = lane & 3;
+            const uint4 v = *reinterpret_cast<const uint4*>(buf + 64 * rr + 16 * (u ^ ((rr >> 1) & 3)));
+            const int grow = row0 + rr, gcol = n + 8 * u;
+            if (grow >= p.m || gcol >= p.n_out) continue;
+            const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&v);
+            for (int d = 0; d < p.npeers; ++d) {
+                __nv_bfloat16* dst = p.peer_d[d] + (size_t)grow * p.ldd + gcol;
+                if (gcol + 8 <= p.n_out) {
+                    *reinterpret_cast<uint4*>(dst) = v;
+                } else {
+                    for (int i = 0; i < 8 && gcol + i < p.n_out; ++i) dst[i] = vb[i];
+                }
+            }
+        }
     }
 }
 
@@ -954,6 +981,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             }
         }
         ptx::bulk_wait_group_all();  // every lane's stores have read shared memory and written D
+        if (p.npeers > 0) __threadfence_system();  // peer stores visible before the kernel ends
     }
 
     ptx::tc_fence_before();
@@ -1117,7 +1145,7 @@ int max_pairs(K kernel, int smem, int sms) {
 
 template <int BN, int STAGES, bool FUSED = false>
 cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const QuantizeArgs* qa = nullptr,
-                        uint32_t* sync_words = nullptr) {
+                        uint32_t* sync_words = nullptr, void* const* peers = nullptr, int npeers = 0) {
     using C = PairCfg<BN, STAGES>;
     auto kernel = nvf4_gemm_pair_kernel<BN, STAGES, FUSED>;
     static std::once_flag attr_once[64];
@@ -1138,6 +1166,11 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const Q
     const bool no_c = !g.c || g.beta == 0.0f;
     const bool d_ok = (reinterpret_cast<uintptr_t>(g.d) & 15) == 0 && g.ldd % 8 == 0;
     if (no_c && d_ok && make_output_map(&md, g.d, g.m, g.n_out, g.ldd)) p.tma_store = 1;
+    if (npeers > 0) {
+        if (!p.tma_store || npeers > kMaxPeers) return cudaErrorNotSupported;
+        for (int i = 0; i < npeers; ++i) p.peer_d[i] = static_cast<__nv_bfloat16*>(peers[i]);
+        p.npeers = npeers;
+    }
     if constexpr (FUSED) {
         p.qtab = quant_tables_device();
         if (!p.qtab || !qa || !sync_words) return cudaErrorInvalidValue;
@@ -1225,6 +1258,21 @@ cudaError_t gemm_launch_fused(const GemmArgs& g, const QuantizeArgs& qa, uint32_
         case 256: return launch_pair<256, 5, true>(g, stream, sms, &qa, sync_words);
         case 192: return launch_pair<192, 6, true>(g, stream, sms, &qa, sync_words);
         case 128: return launch_pair<128, 7, true>(g, stream, sms, &qa, sync_words);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t gemm_launch_peers(const GemmArgs& g, void* const* peers, int npeers, cudaStream_t stream) {
+    if (g.m <= kBM || npeers < 1 || npeers > kMaxPeers) return cudaErrorNotSupported;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const char* force = getenv("FP4B_FORCE_BN");
+    const int bn = force ? atoi(force) : choose_bn_pair(g.m, g.n_out, sms);
+    switch (bn) {
+        case 256: return launch_pair<256, 5, false>(g, stream, sms, nullptr, nullptr, peers, npeers);
+        case 192: return launch_pair<192, 6, false>(g, stream, sms, nullptr, nullptr, peers, npeers);
+        case 128: return launch_pair<128, 7, false>(g, stream, sms, nullptr, nullptr, peers, npeers);
         default: return cudaErrorInvalidValue;
     }
 }

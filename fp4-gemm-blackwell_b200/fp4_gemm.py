@@ -72,6 +72,10 @@ _bind("fp4b_quantize_weights_ex", _vp, [_vp, _i, _i, _i, _vp, _i])
 _bind("fp4b_weight_cache_slice", _vp, [_vp, _i, _i])
 _bind("fp4b_weight_cache_export", _i, [_vp, _vp, _vp, _vp])
 _bind("fp4b_weight_cache_import", _vp, [_vp, _vp, _i, _i, _vp])
+_bind("fp4b_run_cached_peers", _i, [_vp, _i, _i, _i, _vp, _i, _vp, _i, ctypes.POINTER(_vp), _i, _vp, _vp])
+_bind("fp4b_ipc_get_handle", _i, [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_long)])
+_bind("fp4b_ipc_open_handle", _vp, [ctypes.c_char_p, ctypes.c_long])
+_bind("fp4b_ipc_close", _i, [_vp, ctypes.c_long])
 
 # Query scale factor vector size
 SF_VEC_SIZE = _lib.fp4_gemm_sf_vec_size()
@@ -611,3 +615,45 @@ def gemm_prequantized(a_fp4, a_sf, m: int, b_fp4, b_sf, n: int, k_pad: int, bias
 def device_error(clear: bool = True) -> int:
     """Non-zero if a kernel gave up on a bounded wait (synchronises the device)."""
     return _lib.fp4b_device_error(1 if clear else 0)
+
+
+def ipc_handle(t: torch.Tensor):
+    """(64-byte CUDA IPC handle of the allocation holding t, byte offset of t in it)."""
+    buf = ctypes.create_string_buffer(64)
+    off = ctypes.c_long(0)
+    with torch.cuda.device(t.device):
+        if _lib.fp4b_ipc_get_handle(t.data_ptr(), buf, ctypes.byref(off)) != 0:
+            raise RuntimeError(f"fp4b_ipc_get_handle failed ({_last_error()})")
+    return buf.raw, off.value
+
+
+def ipc_open(handle: bytes, offset: int, device) -> int:
+    """Map another process's allocation (see ipc_handle) into this one; returns the address of its tensor."""
+    with torch.cuda.device(device):
+        p = _lib.fp4b_ipc_open_handle(handle, offset)
+    if not p:
+        raise RuntimeError(f"fp4b_ipc_open_handle failed ({_last_error()})")
+    return p
+
+
+def ipc_close(ptr: int, offset: int, device):
+    with torch.cuda.device(device):
+        _lib.fp4b_ipc_close(ptr, offset)
+
+
+def run_cached_peers(x: torch.Tensor, cache: "FP4WeightCache", out: torch.Tensor, peer_ptrs) -> None:
+    """This rank's columns of a column-parallel linear: x [M, K] @ cache^T (+ cache.bias, fused when BF16)
+    into out [M, cols] (a column slice of a [M, N] buffer) and into the same columns of the peers'
+    buffers (device addresses in peer_ptrs, already offset).  Asynchronous; order the ranks afterwards."""
+    x2, lda = _rows_view(x)
+    m, k = x2.shape
+    bias = cache.bias
+    b_ptr = bias.reshape(-1).data_ptr() if (bias is not None and bias.is_cuda and bias.dtype == torch.bfloat16) else None
+    if bias is not None and b_ptr is None:
+        raise ValueError("run_cached_peers fuses the bias: it must be a BF16 CUDA tensor")
+    arr = (_vp * len(peer_ptrs))(*peer_ptrs)
+    with torch.cuda.device(x2.device):
+        rc = _lib.fp4b_run_cached_peers(x2.data_ptr(), m, k, lda, cache._handle, out.shape[1], out.data_ptr(),
+                                        out.stride(0), arr, len(peer_ptrs), b_ptr, _stream_ptr(x2.device))
+    if rc != 0:
+        raise RuntimeError(f"fp4b_run_cached_peers failed with error code {rc} ({_last_error()})")

@@ -10,9 +10,15 @@ single-GPU kernels of ``fp4_gemm``:
 * ``ColumnParallelFP4Linear`` -- the weight is N-sharded: rank p quantizes
   and keeps only its 128-row slice of W (the same bytes as that slice of the
   full cache, because quantization is row-local and scale atoms cover 128
-  rows).  Each rank computes its output columns, then one NCCL all-gather of
-  equal-size, zero-padded slices and a re-layout assemble [M, N] on every
-  rank.
+  rows).  Each rank computes its output columns and the result is assembled
+  as [M, N] on every rank, in one of two ways:
+    - "p2p": the GEMM epilogue itself stores every output tile into the [M, N]
+      buffers of all ranks (CUDA IPC mappings of the peers' buffers, NVLink
+      stores), then a one-element all-reduce on the stream orders the ranks.
+      No gather buffer, no re-layout, the transfer overlaps the tiles.
+    - "nccl": one NCCL all-gather of equal-size, zero-padded slices and a
+      re-layout.  Used when "p2p" does not apply (M <= 128, N not a multiple
+      of 8, a single rank) or when asked for.
 
 Host logic (shard plans, gather and re-layout) is separated from the GPU
 kernels so it can be tested with ``gloo`` process groups on CPU.
@@ -103,24 +109,70 @@ class DataParallelFP4Linear:
         self.cache.free()
 
 
+def peer_targets(peer_bases: dict, rank: int, world: int, buf: int, cap: int, n: int, start: int) -> list:
+    """Device addresses where this rank's first output column lands in every other
+    rank's double buffer [2, cap, n] (BF16): buffer `buf`, row 0, column `start`."""
+    return [peer_bases[q] + 2 * (buf * cap * n + start) for q in range(world) if q != rank]
+
+
 class ColumnParallelFP4Linear:
-    """N-sharded weight cache with an all-gather of the output columns.
+    """N-sharded weight cache; the output columns of all ranks are assembled.
 
     `weight` is the full [N, K] BF16 weight (each rank slices its own rows);
-    the output of ``forward`` is the full [M, N] on every rank."""
+    the output of ``forward`` is the full [M, N] on every rank.  With
+    mode "p2p" (the default where it applies) the result is a view of one of
+    two per-layer buffers that the ranks write into each other: it stays
+    valid until the second following ``forward``."""
 
-    def __init__(self, weight: torch.Tensor, bias: torch.Tensor = None, group=None):
+    def __init__(self, weight: torch.Tensor, bias: torch.Tensor = None, group=None, mode: str = "auto"):
         import fp4_gemm
+        if mode not in ("auto", "p2p", "nccl"):
+            raise ValueError("mode must be 'auto', 'p2p' or 'nccl'")
         self.group = group
+        self.mode = mode
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.n, self.k = weight.shape
+        self.device = weight.device
         self.shards = plan_column_shards(self.n, self.world)
         sh = self.shards[self.rank]
         self.cache = None
         if sh.cols > 0:
             b = bias[sh.start:sh.stop] if bias is not None else None
             self.cache = fp4_gemm.FP4WeightCache(weight[sh.start:sh.stop], b)
+        self._bias_ok = bias is None or bias.dtype == torch.bfloat16  # p2p fuses a BF16 bias
+        self._bufs = None       # [2, cap, N] BF16, written by every rank
+        self._peer_bases = {}   # rank -> (address of its _bufs in this process, IPC offset)
+        self._flip = 0
+        self._flag = None
+
+    def uses_p2p(self, m: int) -> bool:
+        """Same answer on every rank for the same M (the ranks must agree)."""
+        if self.mode == "nccl" or self.world == 1:
+            return False
+        return m > 128 and self.n % 8 == 0 and self.device.type == "cuda" and self._bias_ok
+
+    def _ensure_buffers(self, m: int):
+        import fp4_gemm
+        if self._bufs is not None and self._bufs.shape[1] >= m:
+            return
+        self._close_peers()
+        cap = ((m + 127) // 128) * 128
+        self._bufs = torch.empty(2, cap, self.n, dtype=torch.bfloat16, device=self.device)
+        self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+        mine = fp4_gemm.ipc_handle(self._bufs)
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, (mine[0], mine[1], cap), group=self.group)
+        assert all(e[2] == cap for e in everyone), "ranks disagree on the batch size"
+        for q, (h, off, _) in enumerate(everyone):
+            if q != self.rank:
+                self._peer_bases[q] = (fp4_gemm.ipc_open(h, off, self.device), off)
+
+    def _close_peers(self):
+        import fp4_gemm
+        for ptr, off in self._peer_bases.values():
+            fp4_gemm.ipc_close(ptr, off, self.device)
+        self._peer_bases = {}
 
     def local_forward(self, x: torch.Tensor) -> torch.Tensor:
         sh = self.shards[self.rank]
@@ -130,9 +182,30 @@ class ColumnParallelFP4Linear:
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         lead = x.shape[:-1]
-        out = gather_columns(self.local_forward(x), self.shards, self.group)
+        x2 = x.reshape(-1, self.k)
+        m = x2.shape[0]
+        if not self.uses_p2p(m):
+            out = gather_columns(self.local_forward(x2), self.shards, self.group)
+            return out.reshape(*lead, self.n)
+        import fp4_gemm
+        self._ensure_buffers(m)
+        self._flip ^= 1
+        cap = self._bufs.shape[1]
+        out = self._bufs[self._flip, :m]
+        sh = self.shards[self.rank]
+        if sh.cols > 0:
+            bases = {q: b for q, (b, _) in self._peer_bases.items()}
+            peers = peer_targets(bases, self.rank, self.world, self._flip, cap, self.n, sh.start)
+            fp4_gemm.run_cached_peers(x2, self.cache, out[:, sh.start:sh.stop], peers)
+        # Every rank's tiles are in every buffer once all ranks have passed this point.
+        dist.all_reduce(self._flag, group=self.group)
         return out.reshape(*lead, self.n)
 
     def free(self):
+        if self._bufs is not None:
+            torch.cuda.synchronize(self.device)
+            self._close_peers()
+            dist.barrier(group=self.group)  # no rank still maps this rank's buffers
+            self._bufs = None
         if self.cache is not None:
             self.cache.free()

@@ -171,6 +171,25 @@ int fp4b_run_cached_noalloc(const void* A_bf16, int m, int k_in, int lda, const 
                             const void* C_bf16, int ldc, void* D_bf16, int ldd, const void* bias_bf16, float alpha,
                             float beta, void* stream);
 
+/* Column-parallel cached linear (no counterpart in the reference, which runs
+ * on one device): this rank's output columns [m, n_out] are written to D and,
+ * by the GEMM epilogue itself, to the npeers (1..7) buffers peer_d[] (other
+ * GPUs' [.., ldd] BF16 outputs mapped with fp4b_ipc_open_handle, each already
+ * offset to this rank's first column) with NVLink stores.  The caller orders
+ * the ranks after the call (for example with a one-element all-reduce on the
+ * same stream).  m > 128, no C, 16-byte aligned output rows.  Asynchronous on
+ * `stream`; return codes as fp4b_run_cached_ex. */
+int fp4b_run_cached_peers(const void* A_bf16, int m, int k_in, int lda, const void* cache_handle, int n_out,
+                          void* D_bf16, int ldd, void* const* peer_d, int npeers, const void* bias_bf16,
+                          void* stream);
+
+/* CUDA IPC for the peer buffers (no counterpart in the reference): the 64-byte
+ * handle of the allocation holding `ptr` and ptr's offset in it; opening maps
+ * another process's allocation into this one and returns base + offset. */
+int fp4b_ipc_get_handle(const void* ptr, void* handle_out, long* offset_out);
+void* fp4b_ipc_open_handle(const void* handle, long offset);
+int fp4b_ipc_close(void* ptr, long offset);
+
 #ifdef __cplusplus
 }
 #endif

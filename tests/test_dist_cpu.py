@@ -36,6 +36,14 @@ def test_row_range_partitions_batch():
             assert all(p0 % D.TILE == 0 or p0 == p1 for p0, p1 in parts)
 
 
+def test_peer_targets_address_columns_in_peer_buffers():
+    # bases of the peers' [2, cap, n] BF16 buffers; buffer 1, column 384
+    bases = {0: 1 << 20, 2: 3 << 20, 3: 4 << 20}
+    got = D.peer_targets(bases, rank=1, world=4, buf=1, cap=256, n=2880, start=384)
+    step = 2 * (256 * 2880 + 384)
+    assert got == [(1 << 20) + step, (3 << 20) + step, (4 << 20) + step]
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

@@ -40,6 +40,18 @@ def _worker(rank, world, port, q):
         single = fp4_gemm.FP4WeightCache(wd, bd)
         ref = single.forward(xd)
         assert_gemm_close(y, ref.float(), f"column-parallel rank {rank}")
+        # Column tiles of a shard run the same MMAs as in the full GEMM: both
+        # assembly modes give the single-GPU bytes exactly.
+        assert tp.uses_p2p(m)
+        assert torch.equal(y, ref), "p2p column-parallel differs from one GPU"
+        y2 = tp.forward(xd[:384])  # second buffer, fewer rows
+        assert torch.equal(y2, single.forward(xd[:384]))
+        assert torch.equal(tp.forward(xd), ref)  # first buffer again
+        nc = D.ColumnParallelFP4Linear(wd, bd, mode="nccl")
+        assert torch.equal(nc.forward(xd), ref)
+        small = tp.forward(xd[:100])  # M <= 128 takes the all-gather path
+        assert torch.equal(small, single.forward(xd[:100]))
+        nc.free()
         r0, r1 = D.row_range(m, world, rank)
         dp = D.DataParallelFP4Linear(wd, bd)
         yl = dp.forward(xd[r0:r1], sync=True)
