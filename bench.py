@@ -489,15 +489,110 @@ def run_ours(args):
         print(json.dumps(result), flush=True)
 
 
+# ------------------------------------------------------------------------------ config 5: decoder stack
+STACK_LINEARS = (("qkv", 5120, 2880), ("o", 2880, 4096), ("gate_up", 15360, 2880), ("down", 2880, 7680))
+
+
+def run_stack(args):
+    """Config 5: 12 decoder layers x {QKV 2880->5120, O 4096->2880, gate_up
+    2880->15360, down 7680->2880} on M=8192 tokens, weights N(0,0.02) cached
+    as NVFP4, activations N(0,1) fed fresh to every linear (the shapes do not
+    chain).  tp: every linear column-parallel over the ranks, output
+    assembled on every rank (--tp-mode p2p: the GEMM epilogue stores into all
+    ranks' buffers; nccl: all-gather).  dp: the 8192 rows split over the
+    ranks, weights replicated, no collective."""
+    import datetime
+
+    import torch.distributed as dist
+
+    import fp4_gemm
+    import fp4_gemm_dist as D
+
+    ws, rank, local = dist_env()
+    dev = torch.device("cuda", local if ws > 1 else 0)
+    torch.cuda.set_device(dev)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    m_total = 8192
+    r0, r1 = D.row_range(m_total, ws, rank) if args.stack_mode == "dp" else (0, m_total)
+    m = r1 - r0
+    layers = []
+    g = torch.Generator(device=dev)
+    for li in range(args.layers):
+        lin = []
+        for j, (name, n, k) in enumerate(STACK_LINEARS):
+            g.manual_seed(1000 * li + j)
+            w = (torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            if args.stack_mode == "tp" and ws > 1:
+                lin.append(D.ColumnParallelFP4Linear(w, None, mode=args.tp_mode))
+            else:
+                lin.append(fp4_gemm.FP4WeightCache(w))
+            del w
+        layers.append(lin)
+    g.manual_seed(7)
+    xs = {k: torch.randn(m_total, k, generator=g, device=dev).to(torch.bfloat16)[r0:r1]
+          for k in sorted({k for _, _, k in STACK_LINEARS})}
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for lin in layers:
+            for mod, (_, _, k) in zip(lin, STACK_LINEARS):
+                if isinstance(mod, D.ColumnParallelFP4Linear):
+                    mod.forward(xs[k])
+                else:
+                    mod.forward(xs[k], sync=False)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    if ws > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    flops = 2.0 * m_total * args.layers * sum(n * k for _, n, k in STACK_LINEARS)
+    if rank == 0:
+        par = (f"tp{ws} ({args.tp_mode})" if args.stack_mode == "tp" and ws > 1 else
+               f"dp{ws} (M-split, no collective)")
+        print(json.dumps({
+            "metric": "decoder-stack TFLOPS (config 5)", "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOPS",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "dtype": "nvfp4", "data": "synthetic",
+            "config": {"workload": f"{args.layers} layers x (QKV 2880->5120, O 4096->2880, gate_up 2880->15360, "
+                                   f"down 7680->2880), M={m_total} tokens, fresh activations per linear",
+                       "parallelism": par, "tflop_per_step": flops / 1e12}}), flush=True)
+    for lin in layers:
+        for mod in lin:
+            mod.free()
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=["headline", "stack"], default="headline",
+                    help="stack: config 5 decoder-layer linear stack (not the headline metric)")
+    ap.add_argument("--stack-mode", choices=["tp", "dp"], default="tp")
+    ap.add_argument("--tp-mode", choices=["p2p", "nccl"], default="p2p")
+    ap.add_argument("--layers", type=int, default=12)
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
-    if args.impl == "reference":
+    if args.config == "stack":
+        run_stack(args)
+    elif args.impl == "reference":
         run_reference_arm(args)
     else:
         run_ours(args)
