@@ -1219,17 +1219,25 @@ int choose_bn(long m, long n, int sms) {
     return best;
 }
 
-// The same for 256-row tiles on sms/2 CTA pairs.
-int choose_bn_pair(long m, long n, int sms) {
+// Tile width of the CTA-pair kernel: the one with the smallest modelled time,
+// waves x (stages x stage time + per-tile overhead), fitted to B200 runs of this
+// kernel: a 256-row stage of K = 256 takes about 0.16 + 0.0012 * BN us (the
+// TMA ring's throughput, 0.30 / 0.37 / 0.46 us for BN = 128 / 192 / 256), a
+// tile adds ~2 us (pipeline fill, exposed epilogue), and BN = 256 another
+// ~1.5 us because its accumulator is not double-buffered.
+int choose_bn_pair(long m, long n, long k_pad, int sms) {
     static const int cands[] = {256, 192, 128};
     const long mt = (m + 2 * kBM - 1) / (2 * kBM);
     const long pairs = sms / 2 > 0 ? sms / 2 : 1;
+    const double stages = (double)k_pad / 256.0;
     int best = 128;
-    long best_cost = -1;
+    double best_cost = -1.0;
     for (int bn : cands) {
         const long tiles = mt * ((n + bn - 1) / bn);
-        const long cost = ((tiles + pairs - 1) / pairs) * bn;
-        if (best_cost < 0 || cost < best_cost) {
+        const long waves = (tiles + pairs - 1) / pairs;
+        const double tile = stages * (0.16 + 0.0012 * bn) + 2.0 + (bn == 256 ? 1.5 : 0.0);
+        const double cost = (double)waves * tile;
+        if (best_cost < 0.0 || cost < best_cost) {
             best_cost = cost;
             best = bn;
         }
@@ -1253,7 +1261,7 @@ cudaError_t gemm_launch_fused(const GemmArgs& g, const QuantizeArgs& qa, uint32_
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const char* force = getenv("FP4B_FORCE_BN");
-    const int bn = force ? atoi(force) : choose_bn_pair(g.m, g.n_out, sms);
+    const int bn = force ? atoi(force) : choose_bn_pair(g.m, g.n_out, g.k_pad, sms);
     switch (bn) {
         case 256: return launch_pair<256, 5, true>(g, stream, sms, &qa, sync_words);
         case 192: return launch_pair<192, 6, true>(g, stream, sms, &qa, sync_words);
@@ -1268,7 +1276,7 @@ cudaError_t gemm_launch_peers(const GemmArgs& g, void* const* peers, int npeers,
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const char* force = getenv("FP4B_FORCE_BN");
-    const int bn = force ? atoi(force) : choose_bn_pair(g.m, g.n_out, sms);
+    const int bn = force ? atoi(force) : choose_bn_pair(g.m, g.n_out, g.k_pad, sms);
     switch (bn) {
         case 256: return launch_pair<256, 5, false>(g, stream, sms, nullptr, nullptr, peers, npeers);
         case 192: return launch_pair<192, 6, false>(g, stream, sms, nullptr, nullptr, peers, npeers);
@@ -1301,7 +1309,7 @@ cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     const bool pair = pair_env ? atoi(pair_env) != 0 : g.m > kBM;
     if (pair) {
         const char* force = getenv("FP4B_FORCE_BN");
-        const int bn = force ? atoi(force) : choose_bn_pair(g.m, g.n_out, sms);
+        const int bn = force ? atoi(force) : choose_bn_pair(g.m, g.n_out, g.k_pad, sms);
         switch (bn) {
             case 256: return launch_pair<256, 5, false>(g, stream, sms);
             case 192: return launch_pair<192, 6, false>(g, stream, sms);
