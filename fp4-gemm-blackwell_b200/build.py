@@ -19,7 +19,7 @@ LIB = os.path.join(HERE, "libfp4gemm.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
 SOURCES = ["capi.cu", "quantize.cu", "gemm_sm100.cu", "noalloc.cu"]
-HEADERS = ["fp4b_internal.h", "nvfp4_codec.cuh", "ptx_sm100.cuh"]
+HEADERS = ["fp4b_internal.h", "nvfp4_codec.cuh", "ptx_sm100.cuh", "quantize_core.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -357,6 +357,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Launched behind the activation quantizer: barriers and TMEM are set up
     // while it finishes; no global memory is touched before this point.
     ptx::grid_dependency_wait();
+    // The kernel after this one (the next quantizer) may be scheduled on SMs
+    // this grid leaves; it waits for this grid to complete before it reads or
+    // writes global memory.
+    ptx::launch_dependents();
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -760,6 +764,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     // Launched behind the activation quantizer: barriers and TMEM are set up
     // while it finishes; no global memory is touched before this point.
     ptx::grid_dependency_wait();
+    // The kernel after this one (the next quantizer) may be scheduled on SMs
+    // this grid leaves; it waits for this grid to complete before it reads or
+    // writes global memory.
+    ptx::launch_dependents();
 
     if (warp >= kPairFirstProducer) {
         // ------------------------------------------------------------ producers (both CTAs)

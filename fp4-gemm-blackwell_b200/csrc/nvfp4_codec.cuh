@@ -23,11 +23,10 @@ namespace fp4b {
 constexpr int kSfVec = 16;                  // elements per scale factor
 constexpr float kScaleMin = 1.953125e-3f;   // 2^-9, smallest UE4M3 subnormal
 constexpr float kScaleMax = 480.0f;         // largest UE4M3 value
-// Blocks whose |x|max (as bf16 bits) is below this (2^30) keep every scaled
-// value under 2^23, where the table-driven E2M1 rounding is exact.
+// Blocks whose |x|max (as bf16 bits) is below this (2^30) take the GPU
+// quantizer's fast path, which reads the scale byte from a table over these
+// bit patterns; larger, infinite and NaN blocks take the literal path.
 constexpr uint32_t kFastAbsmaxBf16Limit = 0x4E80u;
-// Number of 2^21-wide fp32 bit slots covering all 32-bit patterns.
-constexpr int kE2M1TableSize = 2048;
 
 FP4B_HD uint32_t f32_bits(float f) {
 #ifdef __CUDA_ARCH__
@@ -81,33 +80,6 @@ FP4B_HD uint8_t e2m1_scan(float v) {
         }
     }
     return (uint8_t)(sign | code);
-}
-
-// Fast-path E2M1 table entry for slot t = (bits(v) - 1) >> 21.  The rounding
-// boundaries (0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5) and the sign all sit on
-// 2^21 multiples of the fp32 bit pattern, so every finite |v| < 2^23 in one
-// slot has the same code; the slot's top pattern (t+1) << 21 represents it
-// (t = 1023 is -0.0, t = 2047 is +0.0).
-FP4B_HD uint8_t e2m1_table_entry(uint32_t t) {
-    return e2m1_scan(bits_f32((t + 1u) << 21));
-}
-
-// Bank-spread variant used by the GPU quantizer.  The kernel multiplies by
-// 32 / scale instead of 1 / scale (exact: a power-of-two factor on a product
-// that never underflows to zero for BF16 inputs), so the slots of |v| in
-// (2^-4, 8), i.e. of |v'| = 32|v| in (2, 256), are the bytes of the 4-byte
-// words 128..134 of the table: shared-memory banks 0..6.  The slot index of a
-// negative value has bit 6 flipped (banks 16..22), +0 and -0 land on banks 15
-// and 31, so the lookups of one warp do not conflict.  Entry i holds the code
-// of slot i ^ ((i >> 10) << 6) of 32v, i.e. of v at 1/32 of that slot's top.
-FP4B_HD uint32_t e2m1_banked_index(uint32_t bits_v32) {
-    const uint32_t t = bits_v32 - 1u;
-    return (t ^ ((t >> 4) & 0x08000000u)) >> 21;
-}
-
-FP4B_HD uint8_t e2m1_banked_entry(uint32_t i) {
-    const uint32_t t = i ^ ((i >> 10) << 6);
-    return e2m1_scan(bits_f32((t + 1u) << 21) * 0.03125f);
 }
 
 FP4B_HD uint8_t ue4m3_encode(float val) {

@@ -3,17 +3,18 @@
 // Replaces quantize_bf16_to_fp4_kernel (fp4_gemm_lib.cu:241-286) with the
 // same bytes out:
 //   * one thread per 16-element block, flattened (row, block) index so a warp
-//     reads 1 KB of contiguous BF16 with two 16-byte loads per thread;
+//     reads 1 KB of contiguous BF16 with two 16-byte loads per thread; a
+//     persistent grid with the next block's loads in flight;
 //   * |x|max by bf16x2 max of magnitudes with NaN propagation (a NaN or Inf
 //     sends the block to the literal path); the scale byte
 //     ue4m3(max(|x|max / 6, 2^-9)) from a table over the fast-path |x|max
 //     bit patterns, built on the host with IEEE division; reciprocal table;
-//   * E2M1 rounding by a 2048-entry shared-memory table indexed by the fp32
-//     bit slot of 32*x*inv (e2m1_banked_index), which reproduces the
-//     reference's strict-< nearest-value scan (ties to the lower code, sign
-//     for any value < 0) for every |x*inv| < 2^23 with the lookups of a warp
-//     on distinct banks; blocks that could leave that range (|x|max >= 2^30,
-//     Inf, NaN) take a literal scan instead;
+//   * E2M1 rounding by the hardware conversion (cvt.rn.satfinite.e2m1x2)
+//     applied to a stand-in for each scaled value that is never a tie and
+//     rounds to the reference's code (e2m1_stand_in in quantize_core.cuh), so
+//     the reference's strict-< nearest-value scan (ties to the lower code,
+//     sign for any value < 0) is reproduced bit for bit; blocks with
+//     |x|max >= 2^30, Inf or NaN take a literal scan instead;
 //   * packed codes written as one 8-byte store per thread, scales gathered
 //     over 4 lanes into one 4-byte store into the 128x4 interleaved layout.
 // HBM-bound: 2 + 0.5 + 1/16 bytes per element.
@@ -45,46 +46,55 @@ bool g_qtab_ready[64];
 const QuantTables& host_tables() {
     static const QuantTables t = [] {
         QuantTables q{};
-        for (uint32_t i = 0; i < (uint32_t)kE2M1TableSize; ++i) q.e2m1[i] = e2m1_banked_entry(i);
         for (int i = 0; i < kScaleTableSize; ++i) {
             // The reference: scale = absmax / 6 in fp32, clamped to [2^-9, 480], UE4M3.
             const float amax = bits_f32((kScaleClampBf16 + (uint32_t)i) << 16);
             q.sbyte[i] = ue4m3_encode(amax / 6.0f);
         }
-        for (int b = 0; b < 128; ++b) q.rcp32[b] = 32.0f * (1.0f / ue4m3_decode((uint8_t)b));
+        for (int b = 0; b < 128; ++b) q.rcp[b] = 1.0f / ue4m3_decode((uint8_t)b);
         return q;
     }();
     return t;
 }
 
-// Grid-stride over spans of 512 blocks (one thread per block, two blocks per
-// thread per span), so the CTAs running at one time read neighbouring memory.
-// The first loads go out before the tables are copied to shared memory, so
-// their latencies overlap.
-__global__ void __launch_bounds__(kThreads) nvfp4_quantize_kernel(const __grid_constant__ QuantParams p) {
+// Persistent grid (as many CTAs as fit on the device at once): thread i
+// quantizes blocks i, i + T, i + 2T, ... (T threads in the grid), so a warp
+// reads 1 KB of contiguous BF16 per block and all resident threads together
+// read one contiguous stretch.  The loads of a thread's next block are in
+// flight while it quantizes the current one (two register sets used in turn),
+// and the first loads go out before the tables are copied to shared memory.
+// Launched with programmatic stream serialization behind a GEMM that may
+// still read this kernel's output buffers: nothing in global memory is read
+// or written before grid_dependency_wait.
+__global__ void __launch_bounds__(kThreads, 6) nvfp4_quantize_kernel(const __grid_constant__ QuantParams p) {
     __shared__ __align__(16) uint8_t s_tables[kSmemTableBytes];
 
-    constexpr uint32_t kSpan = kThreads * kBlocksPerThread;
     const uint32_t lane = threadIdx.x & 31u;
     const uint32_t end = p.total;
-    const uint32_t stride = gridDim.x * kSpan;
-    uint32_t base = blockIdx.x * kSpan;
-    uint32_t w0[8], w1[8], r0, kb0, r1, kb1;
-    load_block(p, base + threadIdx.x, end, w0, r0, kb0);
-    load_block(p, base + threadIdx.x + kThreads, end, w1, r1, kb1);
+    const uint32_t stride = gridDim.x * kThreads;
+    uint32_t idx = blockIdx.x * kThreads + threadIdx.x;
+    uint32_t wa[8], wb[8], ra, kba, rb = 0, kbb = 0;
+    ptx::grid_dependency_wait();
+    load_block(p, idx, end, wa, ra, kba);
     const SmemTables tab = copy_tables(&g_qtab, s_tables, threadIdx.x, kThreads);
     __syncthreads();
     // A GEMM launched behind this kernel may start setting up (it waits for
     // this grid to complete before reading the quantized activations).
     ptx::launch_dependents();
 
+    // Whether the warp's first lane has a block at idx + stride: warp-uniform,
+    // as the scale bytes are gathered with shuffles.
     for (;;) {
-        quantize_and_store(p, base + threadIdx.x, end, w0, r0, kb0, lane, tab);
-        quantize_and_store(p, base + threadIdx.x + kThreads, end, w1, r1, kb1, lane, tab);
-        base += stride;
-        if (base >= end) break;
-        load_block(p, base + threadIdx.x, end, w0, r0, kb0);
-        load_block(p, base + threadIdx.x + kThreads, end, w1, r1, kb1);
+        const bool more_b = idx - lane + stride < end;
+        if (more_b) load_block(p, idx + stride, end, wb, rb, kbb);
+        quantize_and_store(p, idx, end, wa, ra, kba, lane, tab);
+        if (!more_b) break;
+        idx += stride;
+        const bool more_a = idx - lane + stride < end;
+        if (more_a) load_block(p, idx + stride, end, wa, ra, kba);
+        quantize_and_store(p, idx, end, wb, rb, kbb, lane, tab);
+        if (!more_a) break;
+        idx += stride;
     }
 }
 
@@ -135,22 +145,37 @@ qcore::QuantParams make_quant_params(const QuantizeArgs& a) {
 
 cudaError_t quantize_launch(const QuantizeArgs& a, cudaStream_t stream) {
     const QuantParams p = make_quant_params(a);
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (!quant_tables_device()) return cudaErrorInvalidValue;
-    // Up to FP4B_QUANT_CTAS_PER_SM (default 16) CTAs per SM, grid-stride beyond.
-    static int per_sm = [] {
+    // Resident CTAs per SM, once per device; FP4B_QUANT_CTAS_PER_SM caps it.
+    static int per_sm_dev[64];
+    static std::once_flag once[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::call_once(once[dev & 63], [&] {
+        int occ = 0, sms = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, nvfp4_quantize_kernel, kThreads, 0) != cudaSuccess ||
+            occ < 1)
+            occ = 1;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         const char* e = getenv("FP4B_QUANT_CTAS_PER_SM");
-        const int v = e ? atoi(e) : 16;
-        return v > 0 ? v : 16;
-    }();
-    const uint32_t span = kThreads * kBlocksPerThread;
-    const uint64_t need = (p.total + span - 1) / span;
-    const uint64_t cap = (uint64_t)sms * (uint64_t)per_sm;
+        if (e && atoi(e) > 0 && atoi(e) < occ) occ = atoi(e);
+        per_sm_dev[dev & 63] = occ * (sms > 0 ? sms : 148);
+    });
+    cudaGetLastError();
+    const uint64_t need = ((uint64_t)p.total + kThreads - 1) / kThreads;
+    const uint64_t cap = (uint64_t)per_sm_dev[dev & 63];
     const uint64_t grid = need < cap ? need : cap;
-    nvfp4_quantize_kernel<<<(uint32_t)grid, kThreads, 0, stream>>>(p);
-    return cudaGetLastError();
+    if (grid == 0) return cudaSuccess;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((uint32_t)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, nvfp4_quantize_kernel, p);
 }
 
 }  // namespace fp4b

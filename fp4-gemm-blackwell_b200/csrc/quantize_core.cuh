@@ -18,9 +18,8 @@ constexpr uint32_t kScaleClampBf16 = 0x3C40u;
 constexpr int kScaleTableSize = (int)(kFastAbsmaxBf16Limit - kScaleClampBf16);  // 4672
 
 struct QuantTables {
-    uint8_t e2m1[kE2M1TableSize];    // code by bank-spread fp32 bit slot of 32v (e2m1_banked_entry)
     uint8_t sbyte[kScaleTableSize];  // scale byte for |x|max bits kScaleClampBf16 + i
-    float rcp32[128];                // 32 * RN(1 / ue4m3_decode(byte)) (exact power-of-two factor)
+    float rcp[128];                  // RN(1 / ue4m3_decode(byte))
 };
 static_assert(kScaleTableSize % 16 == 0, "tables are copied in 16-byte pieces");
 
@@ -38,13 +37,12 @@ struct QuantParams {
 
 // Shared-memory copies of the tables (copy_tables fills them).
 struct SmemTables {
-    const uint8_t* e2m1;
     const uint8_t* sbyte;
-    const float* rcp32;
+    const float* rcp;
 };
 
 // Bytes of shared memory copy_tables needs (16-byte aligned start).
-constexpr int kSmemTableBytes = kE2M1TableSize + kScaleTableSize + 128 * 4;
+constexpr int kSmemTableBytes = kScaleTableSize + 128 * 4;
 
 // Threads [0, nthreads) of the caller copy the tables from global memory into
 // `smem` (kSmemTableBytes, 16-byte aligned); the caller synchronizes after.
@@ -53,7 +51,7 @@ __device__ __forceinline__ SmemTables copy_tables(const QuantTables* g, uint8_t*
     uint4* dst = reinterpret_cast<uint4*>(smem);
     static_assert(sizeof(QuantTables) == kSmemTableBytes, "table layout");
     for (int i = tid; i < kSmemTableBytes / 16; i += nthreads) dst[i] = __ldg(src + i);
-    return SmemTables{smem, smem + kE2M1TableSize, reinterpret_cast<const float*>(smem + kE2M1TableSize + kScaleTableSize)};
+    return SmemTables{smem, reinterpret_cast<const float*>(smem + kScaleTableSize)};
 }
 
 // Round-up multiplier for exact unsigned division of n < 2^31 by d >= 1.
@@ -64,18 +62,45 @@ inline void make_fast_div(uint32_t d, uint32_t* mul, uint32_t* shift) {
     *mul = (uint32_t)(((1ull << 32) * ((1ull << s) - d)) / d + 1);
 }
 
-// inv32 = 32 * RN(1 / scale): RN(x * inv32) = 32 * RN(x * RN(1 / scale)) whenever
-// the latter is a normal float; when it is not, |v| < 2^-126 and both give
-// code 0 with the same sign (no BF16 x underflows to zero here).
-__device__ __forceinline__ uint32_t e2m1_fast(float x, float inv32, const uint8_t* tab) {
-    return tab[e2m1_banked_index(__float_as_uint(__fmul_rn(x, inv32)))];
+// E2M1 rounding.  The reference scans {0, .5, 1, 1.5, 2, 3, 4, 6} for the
+// nearest value with a strict <, so a tie keeps the lower magnitude, and sets
+// the sign for any v < 0 (fp4_gemm_lib.cu:110-124).  The hardware conversion
+// (cvt.rn.satfinite.e2m1x2.f32) rounds to nearest even, which differs only on
+// ties (0.75, 1.75 and 3.5 go up) and on -0.  So it is applied to a stand-in
+// for v that is never a tie and rounds like v under the reference's rule:
+//   * v = fma(x, inv, +0) is RN(x * inv), except that -0 becomes +0;
+//   * with b the bits of v, (b - 1) | 1 is b itself when b is odd (not a tie:
+//     ties have at least 21 trailing zero bits) and otherwise the float one
+//     ulp closer to zero, which has the same nearest value as v unless v is a
+//     tie, where it has the lower one; the sign is unchanged;
+//   * max(b, 1) maps +0 to the smallest denormal, which converts to +0.
+__device__ __forceinline__ float e2m1_stand_in(float x, float inv) {
+    const uint32_t b = __float_as_uint(__fmaf_rn(x, inv, 0.0f));
+    return __uint_as_float((max(b, 1u) - 1u) | 1u);
 }
 
-// Two packed BF16 -> byte of two E2M1 codes (low element in the low nibble).
-__device__ __forceinline__ uint32_t pack_pair_fast(uint32_t w, float inv32, const uint8_t* tab) {
-    const uint32_t lo = e2m1_fast(__uint_as_float(w << 16), inv32, tab);
-    const uint32_t hi = e2m1_fast(__uint_as_float(w & 0xFFFF0000u), inv32, tab);
-    return lo | (hi << 4);
+// Eight elements (four packed BF16 pairs, low element first) -> one word of
+// eight E2M1 codes, element 2i in the low nibble of byte i.
+__device__ __forceinline__ uint32_t pack8_e2m1(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, float inv) {
+    uint32_t out;
+    asm("{\n"
+        ".reg .b8 b0, b1, b2, b3;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n"
+        "mov.b32 %0, {b0, b1, b2, b3};\n"
+        "}"
+        : "=r"(out)
+        : "f"(e2m1_stand_in(__uint_as_float(w0 << 16), inv)),
+          "f"(e2m1_stand_in(__uint_as_float(w0 & 0xFFFF0000u), inv)),
+          "f"(e2m1_stand_in(__uint_as_float(w1 << 16), inv)),
+          "f"(e2m1_stand_in(__uint_as_float(w1 & 0xFFFF0000u), inv)),
+          "f"(e2m1_stand_in(__uint_as_float(w2 << 16), inv)),
+          "f"(e2m1_stand_in(__uint_as_float(w2 & 0xFFFF0000u), inv)),
+          "f"(e2m1_stand_in(__uint_as_float(w3 << 16), inv)),
+          "f"(e2m1_stand_in(__uint_as_float(w3 & 0xFFFF0000u), inv)));
+    return out;
 }
 
 // Element load with zero padding outside [rows, cols).
@@ -129,7 +154,6 @@ __device__ __forceinline__ uint32_t max_abs_bf16x2(uint32_t a, uint32_t b) {
 }
 
 constexpr int kThreads = 256;
-constexpr int kBlocksPerThread = 2;  // 16-element blocks per thread per loop trip
 
 // Scale byte of a block from its |x|max (bf16 bits < kFastAbsmaxBf16Limit);
 // below 6 * 2^-9 the reference clamps the scale to 2^-9 (byte 0x01).
@@ -164,15 +188,12 @@ __device__ __forceinline__ void quantize_and_store(const QuantParams& p, uint32_
     const uint32_t mx = max_abs_bf16x2(max_abs_bf16x2(m01, m23), max_abs_bf16x2(m45, m67));
     const uint32_t amax_bits = max(mx & 0x7FFFu, (mx >> 16) & 0x7FFFu);
 
-    uint32_t sbyte, out0 = 0, out1 = 0;
+    uint32_t sbyte, out0, out1;
     if (amax_bits < kFastAbsmaxBf16Limit) {
         sbyte = scale_byte(amax_bits, tab.sbyte);
-        const float inv32 = tab.rcp32[sbyte];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            out0 |= pack_pair_fast(w[i], inv32, tab.e2m1) << (8 * i);
-            out1 |= pack_pair_fast(w[i + 4], inv32, tab.e2m1) << (8 * i);
-        }
+        const float inv = tab.rcp[sbyte];
+        out0 = pack8_e2m1(w[0], w[1], w[2], w[3], inv);
+        out1 = pack8_e2m1(w[4], w[5], w[6], w[7], inv);
     } else {
         const BlockOut o = quantize_block_exact(p.src, p.ld, p.rows, p.cols, r, kb * kSfVec);
         sbyte = o.sbyte;
