@@ -98,6 +98,111 @@ __global__ void __launch_bounds__(kThreads, 6) nvfp4_quantize_kernel(const __gri
     }
 }
 
+// Staged variant for dense inputs (rows stored back to back, ld == cols ==
+// padded K, 16-byte aligned): the blocks of rows [0, rows) are one contiguous
+// array of 32-byte blocks, so span j (blocks 256j .. 256j + 255, 8 KB) is one
+// 1-D bulk copy.  A producer warp streams the spans of this CTA (j = CTA,
+// CTA + G, ...) into a ring of shared-memory stages with cp.async.bulk;
+// eight consumer warps quantize one block per thread from shared memory and
+// release the stage.  Five CTAs per SM keep 160 KB of input in flight per SM
+// with no registers spent on it.  Blocks of the padding rows are zeros.
+constexpr int kStagedWarps = 8;
+constexpr int kStagedThreads = (kStagedWarps + 1) * 32;
+constexpr int kSpanBlocks = kStagedWarps * 32;
+constexpr int kSpanBytes = kSpanBlocks * 32;
+constexpr int kStagedStages = 4;
+constexpr int kErrQuantStageTimeout = 5;  // device error word: a quantizer ring wait gave up
+constexpr uint64_t kQuantDrainNs = 200000;  // after a timeout, let issued copies land
+
+__global__ void __launch_bounds__(kStagedThreads, 5)
+    nvfp4_quantize_staged_kernel(const __grid_constant__ QuantParams p, int* err) {
+    __shared__ __align__(128) uint8_t s_stage[kStagedStages][kSpanBytes];
+    __shared__ __align__(16) uint8_t s_tables[kSmemTableBytes];
+    __shared__ __align__(8) uint64_t full[kStagedStages], empty[kStagedStages];
+    __shared__ int s_abort;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t nspans = (p.total + kSpanBlocks - 1) / kSpanBlocks;
+    const uint32_t dense = p.rows * p.nsb;  // blocks stored in memory
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStagedStages; ++i) {
+            ptx::mbar_init(&full[i], 1);
+            ptx::mbar_init(&empty[i], kStagedWarps);
+        }
+        s_abort = 0;
+        ptx::fence_mbar_init();
+    }
+    const SmemTables tab = copy_tables(&g_qtab, s_tables, threadIdx.x, kStagedThreads);
+    __syncthreads();
+    // The input may be the output of the kernel before this one, and that
+    // kernel may still read the buffers this one writes.
+    ptx::grid_dependency_wait();
+    ptx::launch_dependents();
+
+    bool timed_out = false;
+    if (warp == kStagedWarps) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            uint32_t k = 0;
+            for (uint32_t span = blockIdx.x; span < nspans; span += gridDim.x, ++k) {
+                const uint32_t s = k % kStagedStages;
+                if (k >= kStagedStages && !ptx::mbar_wait(&empty[s], ((k / kStagedStages) - 1) & 1)) {
+                    timed_out = true;
+                    break;
+                }
+                if (*reinterpret_cast<volatile int*>(&s_abort)) break;
+                const uint32_t b0 = span * kSpanBlocks;
+                const uint32_t nb = dense > b0 ? min((uint32_t)kSpanBlocks, dense - b0) : 0u;
+                if (nb > 0) {
+                    ptx::mbar_arrive_expect_tx(&full[s], nb * 32u);
+                    ptx::bulk_load(s_stage[s], p.src + (size_t)b0 * kSfVec, nb * 32u, &full[s]);
+                } else {
+                    ptx::mbar_arrive(&full[s]);
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ consumers
+        uint32_t k = 0;
+        for (uint32_t span = blockIdx.x; span < nspans; span += gridDim.x, ++k) {
+            const uint32_t s = k % kStagedStages;
+            const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(&full[s], (k / kStagedStages) & 1));
+            if (!ok || *reinterpret_cast<volatile int*>(&s_abort)) {
+                timed_out = !ok;
+                break;
+            }
+            const uint32_t idx = span * kSpanBlocks + threadIdx.x;
+            const uint32_t r = (__umulhi(idx, p.div_mul) + idx) >> p.div_shift;
+            const uint32_t kb = idx - r * p.nsb;
+            uint32_t w[8];
+            if (idx < dense) {
+                const uint4* src = reinterpret_cast<const uint4*>(s_stage[s] + threadIdx.x * 32u);
+                const uint4 v0 = src[0], v1 = src[1];
+                w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
+                w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) w[i] = 0u;
+            }
+            quantize_and_store(p, idx, p.total, w, r, kb, lane, tab);
+            // The stage's bytes were consumed above (the stores depend on them).
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&empty[s]);
+        }
+    }
+    if (timed_out) {
+        if (err) atomicCAS(err, 0, kErrQuantStageTimeout);
+        atomicExch(&s_abort, 1);
+    }
+    __syncthreads();
+    if (s_abort) {
+        // Copies issued before the timeout still land in this CTA's shared memory.
+        const uint64_t t0 = ptx::global_timer_ns();
+        while (ptx::global_timer_ns() - t0 < kQuantDrainNs) {
+        }
+    }
+}
+
 }  // namespace
 
 const qcore::QuantTables* quant_tables_device() {
@@ -143,39 +248,63 @@ qcore::QuantParams make_quant_params(const QuantizeArgs& a) {
     return p;
 }
 
-cudaError_t quantize_launch(const QuantizeArgs& a, cudaStream_t stream) {
-    const QuantParams p = make_quant_params(a);
-    if (!quant_tables_device()) return cudaErrorInvalidValue;
-    // Resident CTAs per SM, once per device; FP4B_QUANT_CTAS_PER_SM caps it.
-    static int per_sm_dev[64];
-    static std::once_flag once[64];
-    int dev = 0;
-    cudaGetDevice(&dev);
-    std::call_once(once[dev & 63], [&] {
-        int occ = 0, sms = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, nvfp4_quantize_kernel, kThreads, 0) != cudaSuccess ||
-            occ < 1)
-            occ = 1;
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        const char* e = getenv("FP4B_QUANT_CTAS_PER_SM");
-        if (e && atoi(e) > 0 && atoi(e) < occ) occ = atoi(e);
-        per_sm_dev[dev & 63] = occ * (sms > 0 ? sms : 148);
-    });
-    cudaGetLastError();
-    const uint64_t need = ((uint64_t)p.total + kThreads - 1) / kThreads;
-    const uint64_t cap = (uint64_t)per_sm_dev[dev & 63];
-    const uint64_t grid = need < cap ? need : cap;
-    if (grid == 0) return cudaSuccess;
+namespace {
+
+// Launch with programmatic stream serialization (the kernels wait for the
+// previous kernel on the stream before touching global memory).
+template <typename K, typename... Args>
+cudaError_t launch_pdl(K kernel, uint32_t grid, uint32_t threads, cudaStream_t stream, Args... args) {
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((uint32_t)grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(threads);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, nvfp4_quantize_kernel, p);
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// Resident CTAs of `kernel` on the current device (once per device and kernel).
+template <typename K>
+int resident_ctas(K kernel, int threads, std::once_flag* once, int* cache) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::call_once(once[dev & 63], [&] {
+        int occ = 0, sms = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, 0) != cudaSuccess || occ < 1) occ = 1;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const char* e = getenv("FP4B_QUANT_CTAS_PER_SM");
+        if (e && atoi(e) > 0 && atoi(e) < occ) occ = atoi(e);
+        cache[dev & 63] = occ * (sms > 0 ? sms : 148);
+    });
+    cudaGetLastError();
+    return cache[dev & 63];
+}
+
+}  // namespace
+
+cudaError_t quantize_launch(const QuantizeArgs& a, cudaStream_t stream) {
+    const QuantParams p = make_quant_params(a);
+    if (!quant_tables_device()) return cudaErrorInvalidValue;
+    if (p.total == 0) return cudaSuccess;
+    // Dense input: rows back to back with no column padding -> staged kernel.
+    const char* staged_env = getenv("FP4B_QUANT_STAGED");
+    const bool staged_ok = staged_env ? atoi(staged_env) != 0 : true;
+    if (staged_ok && p.vec_ok && p.ld == p.cols && p.cols == p.nsb * kSfVec) {
+        static std::once_flag once[64];
+        static int cache[64];
+        const uint64_t need = ((uint64_t)p.total + kSpanBlocks - 1) / kSpanBlocks;
+        const uint64_t cap = (uint64_t)resident_ctas(nvfp4_quantize_staged_kernel, kStagedThreads, once, cache);
+        return launch_pdl(nvfp4_quantize_staged_kernel, (uint32_t)(need < cap ? need : cap), kStagedThreads, stream, p,
+                          device_error_word());
+    }
+    static std::once_flag once[64];
+    static int cache[64];
+    const uint64_t need = ((uint64_t)p.total + kThreads - 1) / kThreads;
+    const uint64_t cap = (uint64_t)resident_ctas(nvfp4_quantize_kernel, kThreads, once, cache);
+    return launch_pdl(nvfp4_quantize_kernel, (uint32_t)(need < cap ? need : cap), kThreads, stream, p);
 }
 
 }  // namespace fp4b
