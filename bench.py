@@ -577,14 +577,53 @@ def run_stack(args):
         dist.destroy_process_group()
 
 
+def run_quantize(args):
+    """Config 4 alone: the standalone quantizer on the 16384 x 16384 Student-t
+    stress tensor (512 MiB in, inputs larger than L2), one JSON line.  The
+    headline run reports the same figure under "quantize"; this entry point
+    exists so that the kernel can be timed or profiled without the rest."""
+    import fp4_gemm
+    from tests import workloads as W
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = fp4_gemm._lib
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+    q4 = W.quantizer_stress(16384, 16384, seed=0).to(dev)
+    q4_fp4 = torch.empty(16384, 8192, dtype=torch.uint8, device=dev)
+    q4_sf = torch.empty(16384 * 1024, dtype=torch.uint8, device=dev)
+
+    def quant4():
+        rc = lib.fp4b_quantize(q4.data_ptr(), 16384, 16384, 16384, q4_fp4.data_ptr(), q4_sf.data_ptr(), 16384,
+                               16384, sptr)
+        if rc != 0:
+            raise RuntimeError(f"fp4b_quantize failed ({rc})")
+    ms = time_rotating([quant4], args.steps, args.warmup, stream)
+    nbytes = 16384 * 16384 * (2 + 0.5 + 0.0625)
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    peaks = load_peaks()
+    peak = peaks["hbm_gbs"]
+    print(json.dumps({"metric": "quantize HBM GB/s (config 4)", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                      "dtype": "bf16->nvfp4", "data": "synthetic",
+                      "config": {"workload": "config 4: 16384x16384 bf16 Student-t stress, bit-exact",
+                                 "l2": "input 512 MiB > L2"},
+                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                                   "frac": gbs / peak, "algorithmic_bytes": nbytes,
+                                   "peak_source": peaks["source"]},
+                      "gpu_launches": args.steps}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["headline", "stack"], default="headline",
-                    help="stack: config 5 decoder-layer linear stack (not the headline metric)")
+    ap.add_argument("--config", choices=["headline", "stack", "quantize"], default="headline",
+                    help="stack: config 5 decoder-layer linear stack; quantize: config 4 quantizer alone "
+                         "(neither is the headline metric)")
     ap.add_argument("--stack-mode", choices=["tp", "dp"], default="tp")
     ap.add_argument("--tp-mode", choices=["p2p", "nccl"], default="p2p")
     ap.add_argument("--layers", type=int, default=12)
@@ -592,6 +631,8 @@ def main():
     args.warmup = max(3, args.warmup)
     if args.config == "stack":
         run_stack(args)
+    elif args.config == "quantize":
+        run_quantize(args)
     elif args.impl == "reference":
         run_reference_arm(args)
     else:
