@@ -587,14 +587,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 // that has not issued for 32 stages.
 constexpr int kPairEpiWarps = 8;  // two per TMEM lane quadrant, each storing half of the columns
 
-template <int BN, int STAGES>
+// A pair tile is 256 x TW with TW = NSUB * BN: NSUB MMAs of N = BN per k-block
+// share the A tile (NSUB = 2 moves a third fewer operand bytes per column; its
+// accumulator is single-buffered, so it suits problems whose tiles fit in one
+// round of CTA pairs).
+template <int BN, int STAGES, int NSUB = 1>
 struct PairCfg {
     static constexpr int kKbPerStage = 4;   // a stage covers K = 256: one 128-byte chunk
     static_assert(BN % 64 == 0 && BN >= 128 && BN <= 256, "BN must be 128, 192 or 256");
-    static constexpr int BH = BN / 2;       // B rows held by each CTA
-    static constexpr int NRT = max_row_tiles(BN);
+    static_assert(NSUB == 1 || NSUB == 2, "one or two MMAs per k-block");
+    static constexpr int TW = NSUB * BN;    // tile width
+    static constexpr int BH = BN / 2;       // B rows of one MMA held by each CTA
+    static constexpr int NRT = max_row_tiles(TW);
     static constexpr int A_BYTES = kBM * kChunkBytes;
-    static constexpr int B_BYTES = BH * kChunkBytes;
+    static constexpr int B_SUB_BYTES = BH * kChunkBytes;
+    static constexpr int B_BYTES = NSUB * B_SUB_BYTES;
     static constexpr int SFA_BYTES = kKbPerStage * kAtomBytes;
     static constexpr int SFB_BYTES = NRT * kKbPerStage * kAtomBytes;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
@@ -604,13 +611,13 @@ struct PairCfg {
     static constexpr int BAR_BYTES = 256;
     // Epilogue staging: one 32 x 32 BF16 buffer (2 KB) and half the tile's bias per epilogue warp.
     static constexpr int EPI_BYTES = kPairEpiWarps * 2048;          // one 32 x 32 BF16 buffer per epilogue warp
-    static constexpr int BIAS_BYTES = kPairEpiWarps * (BN / 2) * 4;  // fp32 bias of each warp's half of the tile
+    static constexpr int BIAS_BYTES = kPairEpiWarps * (TW / 2) * 4;  // fp32 bias of each warp's half of the tile
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + BIAS_BYTES + BAR_BYTES + 1024;
     static constexpr int SF_COLS = 4 * kKbPerStage * (1 + NRT);
-    static constexpr int ACC_BUFS = (2 * BN + SF_COLS <= (int)kTmemCols) ? 2 : 1;
-    static constexpr uint32_t TMEM_SFA = ACC_BUFS * BN;
+    static constexpr int ACC_BUFS = (2 * TW + SF_COLS <= (int)kTmemCols) ? 2 : 1;
+    static constexpr uint32_t TMEM_SFA = ACC_BUFS * TW;
     static constexpr uint32_t TMEM_SFB = TMEM_SFA + 4 * kKbPerStage;
-    static_assert(B_BYTES % 1024 == 0, "B stage must keep the 128B-swizzle alignment");
+    static_assert(B_SUB_BYTES % 1024 == 0, "B stage must keep the 128B-swizzle alignment");
     static_assert(STAGE_BYTES % 1024 == 0, "epilogue buffers must stay 1024-byte aligned");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
     static_assert(TMEM_SFA + SF_COLS <= kTmemCols, "TMEM budget exceeded");
@@ -702,12 +709,13 @@ __device__ __forceinline__ void quantize_phase(const Params& p, const qcore::Sme
     count_tiles(p, lane, counted, p.m_tiles);
 }
 
-template <int BN, int STAGES, bool FUSED>
+template <int BN, int STAGES, bool FUSED, int NSUB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     nvf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
                           const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ Params p) {
-    using C = PairCfg<BN, STAGES>;
+    using C = PairCfg<BN, STAGES, NSUB>;
+    constexpr int TW = C::TW;
     constexpr int TILE_M = 2 * kBM;
     constexpr int kKbPerStage = C::kKbPerStage;
     extern __shared__ uint8_t smem_raw[];
@@ -779,7 +787,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         for (int t = pair; t < p.num_tiles && !stop; t += npairs) {
             int m_tile, n_tile;
             tile_coords(t, p.m_tiles, p.n_tiles, TILE_M, m_tile, n_tile);
-            const int n0 = n_tile * BN;
+            const int n0 = n_tile * TW;
             const int a_row = m_tile * 2 * kBM + (int)rank * kBM;
             const int b_row = n0 + (int)rank * C::BH;
             const int sfa_rt = m_tile * 2 + (int)rank;
@@ -819,7 +827,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                         ready_tile = m_tile;
                     }
                 }
-                if (lane == (it & 31)) {
+                // The B copies of the NSUB MMAs go out from different lanes.
+                const int sub = (NSUB > 1 && role == 1 && lane == ((it + 16) & 31)) ? 1 : 0;
+                if (lane == (it & 31) || sub == 1) {
                     const uint32_t bar = full0 + (uint32_t)s * 8u;
                     const int kx = ks * kChunkBytes;
                     const int kb0 = ks * kKbPerStage;
@@ -827,7 +837,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                         if (rank == 0) ptx::mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
                         ptx::tma_load_2d_pair(sA + s * C::A_BYTES, &tmap_a, bar, kx, a_row);
                     } else if (role == 1) {
-                        ptx::tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_b, bar, kx, b_row);
+                        ptx::tma_load_2d_pair(sB + s * C::B_BYTES + sub * C::B_SUB_BYTES, &tmap_b, bar, kx,
+                                              b_row + sub * BN);
                     } else if (role == 2) {
                         ptx::tma_load_3d_pair(sSFA + s * C::SFA_BYTES, &tmap_sfa, bar, 0, kb0, sfa_rt);
                     } else {
@@ -850,7 +861,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             for (int t = pair; t < p.num_tiles && !stop; t += npairs, ++tile_iter) {
                 int m_tile_unused, n_tile;
                 tile_coords(t, p.m_tiles, p.n_tiles, TILE_M, m_tile_unused, n_tile);
-                const int n0 = n_tile * BN;
+                const int n0 = n_tile * TW;
                 const uint32_t shift_words = (n0 & 127) >> 5;
                 const int b = tile_iter % C::ACC_BUFS;
                 if (tile_iter >= C::ACC_BUFS) {
@@ -865,7 +876,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     }
                 }
                 ptx::tc_fence_after();
-                const uint32_t acc = tmem + b * BN;
+                const uint32_t acc = tmem + b * TW;
                 const uint32_t sfa_t = tmem + C::TMEM_SFA;
                 const uint32_t sfb_t = tmem + C::TMEM_SFB;
                 for (int ks = 0; ks < num_ks; ++ks, ++it) {
@@ -903,8 +914,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                         for (int j = 0; j < kKbPerStage; ++j) {
                             if (j < nkb) {
                                 const uint32_t koff = (uint32_t)((32 * j) >> 4);
-                                ptx::tc_mma_nvf4_pair(acc, a_s + koff, b_s + koff, idesc, sfa_t + 4 * j,
-                                                      sfb_t + j * 4 * C::NRT + shift_words, (j == 0) ? first : 1u);
+#pragma unroll
+                                for (int u = 0; u < NSUB; ++u)
+                                    ptx::tc_mma_nvf4_pair(acc + u * BN, a_s + koff,
+                                                          b_s + (uint64_t)((u * C::B_SUB_BYTES) >> 4) + koff, idesc,
+                                                          sfa_t + 4 * j,
+                                                          sfb_t + j * 4 * C::NRT + shift_words + (u * BN) / 32,
+                                                          (j == 0) ? first : 1u);
                             }
                         }
                         ptx::tc_commit_pair(&empty[s], 0x3);
@@ -923,10 +939,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         // ------------------------------------------------------------ epilogue (both CTAs)
         const int q = warp & 3;   // TMEM lane quadrant
         const int h = warp >> 2;  // chunks c = h, h + 2, ...
-        constexpr int kMyChunks = BN / 64;
+        constexpr int kMyChunks = TW / 64;
         const uint32_t acc_empty0 = ptx::map_to_cta(ptx::smem_u32(acc_empty), 0);
         uint8_t* epi = sEpi + warp * 2048;
-        float4* wbias = sBias + warp * (BN / 8);
+        float4* wbias = sBias + warp * (TW / 8);
         if constexpr (FUSED) {
             // The quantizer tables live in the (not yet used) epilogue staging buffers.
             static_assert(C::EPI_BYTES >= qcore::kSmemTableBytes, "tables must fit the staging buffers");
@@ -940,7 +956,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         for (int t = pair; t < p.num_tiles; t += npairs, ++tile_iter) {
             int m_tile, n_tile;
             tile_coords(t, p.m_tiles, p.n_tiles, TILE_M, m_tile, n_tile);
-            const int n0 = n_tile * BN;
+            const int n0 = n_tile * TW;
             const int m = m_tile * 2 * kBM + (int)rank * kBM + q * 32 + lane;
             const int b = tile_iter % C::ACC_BUFS;
             if (p.bias) {
@@ -961,7 +977,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             // Only a later tile of this pair that reuses accumulator b waits for it.
             const bool release = t + C::ACC_BUFS * npairs < p.num_tiles;
             // The TMEM load of the next chunk is in flight while one is converted and stored.
-            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + b * BN + 32 * h;
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + b * TW + 32 * h;
             uint32_t ra[32], rb[32];
             ptx::tmem_ld_32x32b_x32(tbase, ra);
 #pragma unroll
@@ -1151,11 +1167,11 @@ int max_pairs(K kernel, int smem, int sms) {
     return c;
 }
 
-template <int BN, int STAGES, bool FUSED = false>
+template <int BN, int STAGES, bool FUSED = false, int NSUB = 1>
 cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const QuantizeArgs* qa = nullptr,
                         uint32_t* sync_words = nullptr, void* const* peers = nullptr, int npeers = 0) {
-    using C = PairCfg<BN, STAGES>;
-    auto kernel = nvf4_gemm_pair_kernel<BN, STAGES, FUSED>;
+    using C = PairCfg<BN, STAGES, NSUB>;
+    auto kernel = nvf4_gemm_pair_kernel<BN, STAGES, FUSED, NSUB>;
     static std::once_flag attr_once[64];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1168,7 +1184,7 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const Q
         !make_scale_map(&msa, g.a_sf, g.m_rows_pad, g.k_pad, C::kKbPerStage, 1) ||
         !make_scale_map(&msb, g.b_sf, g.n_rows_pad, g.k_pad, C::kKbPerStage, C::NRT))
         return cudaErrorInvalidValue;
-    Params p = make_params(g, BN, 2 * kBM);
+    Params p = make_params(g, C::TW, 2 * kBM);
     // D through TMA stores when C is not read and D's rows are 16-byte aligned.
     memset(&md, 0, sizeof(md));
     const bool no_c = !g.c || g.beta == 0.0f;
@@ -1228,26 +1244,32 @@ int choose_bn(long m, long n, int sms) {
 }
 
 // Tile width of the CTA-pair kernel: the one with the smallest modelled time,
-// waves x (stages x stage time + per-tile overhead), fitted to B200 runs of this
-// kernel: a 256-row stage of K = 256 takes about 0.16 + 0.0012 * BN us (the
-// TMA ring's throughput, 0.30 / 0.37 / 0.46 us for BN = 128 / 192 / 256), a
-// tile adds ~2 us (pipeline fill, exposed epilogue), and BN = 256 another
-// ~1.5 us because its accumulator is not double-buffered.
+//   rounds x (stages x stage time + per-round overhead) + fixed cost,
+// rounds = ceil(tiles / pairs), a stage = K of 256.  Fitted to back-to-back
+// B200 runs of this kernel on seven shapes from 512x2880x2880 to 8192^3 (each
+// within ~8 % of the fit): stage time 0.30 / 0.37 / 0.44 us for BN = 128 /
+// 192 / 256 (the TMA ring and the tensor pipe, both ~busy) and 0.55 us for the
+// 256 x 384 tile (two N = 192 MMAs per k-block on one A tile: a third fewer
+// operand bytes per column); per-round overhead ~1 us with two accumulators in
+// TMEM (the epilogue overlaps the next tile), 2.1 us for BN = 256 and 4.2 us
+// for the 384-wide tile, whose single accumulator exposes every epilogue.
+// Returns 128, 192, 256 or 384 (= 2 x 192).
 int choose_bn_pair(long m, long n, long k_pad, int sms) {
-    static const int cands[] = {256, 192, 128};
+    struct Width { int code; double stage_us, round_us, fixed_us; };
+    static const Width cands[] = {{384, 0.55, 4.2, 3.0}, {256, 0.44, 2.06, 5.0}, {192, 0.37, 1.0, 5.0},
+                                  {128, 0.30, 1.0, 5.0}};
     const long mt = (m + 2 * kBM - 1) / (2 * kBM);
     const long pairs = sms / 2 > 0 ? sms / 2 : 1;
-    const double stages = (double)k_pad / 256.0;
+    const double stages = (double)((k_pad + 255) / 256);
     int best = 128;
     double best_cost = -1.0;
-    for (int bn : cands) {
-        const long tiles = mt * ((n + bn - 1) / bn);
-        const long waves = (tiles + pairs - 1) / pairs;
-        const double tile = stages * (0.16 + 0.0012 * bn) + 2.0 + (bn == 256 ? 1.5 : 0.0);
-        const double cost = (double)waves * tile;
+    for (const Width& w : cands) {
+        const long tiles = mt * ((n + w.code - 1) / w.code);
+        const long rounds = (tiles + pairs - 1) / pairs;
+        const double cost = (double)rounds * (stages * w.stage_us + w.round_us) + w.fixed_us;
         if (best_cost < 0.0 || cost < best_cost) {
             best_cost = cost;
-            best = bn;
+            best = w.code;
         }
     }
     return best;
@@ -1274,6 +1296,7 @@ cudaError_t gemm_launch_fused(const GemmArgs& g, const QuantizeArgs& qa, uint32_
         case 256: return launch_pair<256, 5, true>(g, stream, sms, &qa, sync_words);
         case 192: return launch_pair<192, 6, true>(g, stream, sms, &qa, sync_words);
         case 128: return launch_pair<128, 7, true>(g, stream, sms, &qa, sync_words);
+        case 384: return launch_pair<192, 6, true>(g, stream, sms, &qa, sync_words);  // no fused 384-wide tile
         default: return cudaErrorInvalidValue;
     }
 }
@@ -1289,6 +1312,7 @@ cudaError_t gemm_launch_peers(const GemmArgs& g, void* const* peers, int npeers,
         case 256: return launch_pair<256, 5, false>(g, stream, sms, nullptr, nullptr, peers, npeers);
         case 192: return launch_pair<192, 6, false>(g, stream, sms, nullptr, nullptr, peers, npeers);
         case 128: return launch_pair<128, 7, false>(g, stream, sms, nullptr, nullptr, peers, npeers);
+        case 384: return launch_pair<192, 4, false, 2>(g, stream, sms, nullptr, nullptr, peers, npeers);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -1322,6 +1346,7 @@ cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream) {
             case 256: return launch_pair<256, 5, false>(g, stream, sms);
             case 192: return launch_pair<192, 6, false>(g, stream, sms);
             case 128: return launch_pair<128, 7, false>(g, stream, sms);
+            case 384: return launch_pair<192, 4, false, 2>(g, stream, sms);
             default: return cudaErrorInvalidValue;
         }
     }

@@ -150,3 +150,24 @@ def test_dequant_torch_matches_oracle(cuda, fp4):
     got = dequant_torch(aq, asf, 256, 384).cpu()
     want = oracle_dequant(aq.cpu().numpy().reshape(-1), asf.cpu().numpy().reshape(-1), 256, 384)
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 384, 512), (300, 1000, 640), (257, 769, 256), (2304, 3200, 512),
+                                   (2048, 2880, 7680)])
+def test_wide_pair_tile_equals_default(cuda, fp4, monkeypatch, m, n, k):
+    # The 256 x 384 pair tile (two N = 192 MMAs per k-block on one A tile, one
+    # TMEM accumulator) runs the same K sequence per output element as the
+    # other widths, so its bytes equal theirs; also close to the oracle, and
+    # several tiles per pair (2304 x 3200) reuse the single accumulator.
+    x = W.normal_bf16((m, k), 1.0, 71)
+    w = W.normal_bf16((n, k), 1.0, 72)
+    b = W.normal_bf16((n,), 1.0, 73)
+    monkeypatch.setenv("FP4B_PAIR", "1")
+    monkeypatch.setenv("FP4B_FORCE_BN", "192")
+    narrow = run_prequant(fp4, x, w, bias=b)
+    monkeypatch.setenv("FP4B_FORCE_BN", "384")
+    wide = run_prequant(fp4, x, w, bias=b)
+    assert torch.equal(wide, narrow)
+    if m * n * k < 1e9:
+        assert_gemm_close(wide, oracle_linear(x, w, bias=b), f"384-wide {m}x{n}x{k}")
+    assert fp4.device_error() == 0
