@@ -235,10 +235,10 @@ __device__ __forceinline__ void stage_bias(const Params& p, float4* dst, int n0,
 // One thread's TMA copies run one after another (~0.4 us each), so chunk i
 // is stored by lane i % 32, and the lane that stored the buffer's previous
 // contents (chunk i - 1) waits until that store has read it.
-__device__ __forceinline__ void stage_chunk_tma(const Params& p, const CUtensorMap* tmap_d, const uint32_t (&r)[32],
-                                                const float4* sbias, uint8_t* buf, int row0, int n, int lane,
-                                                int chunk_iter) {
-    uint32_t packed[16];
+// Accumulator chunk (32 fp32 columns of this lane's row) -> 16 packed BF16
+// pairs: alpha, BF16, then the BF16 bias add of the reference.
+__device__ __forceinline__ void convert_chunk(const Params& p, const uint32_t (&r)[32], const float4* sbias,
+                                              uint32_t (&packed)[16]) {
     float v[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
@@ -262,6 +262,14 @@ __device__ __forceinline__ void stage_chunk_tma(const Params& p, const CUtensorM
             }
         }
     }
+}
+
+// Writes a converted chunk into the warp's 64B-swizzled staging buffer and
+// stores it with one TMA store (issued by a rotating lane), plus the copies to
+// peer GPUs.
+__device__ __forceinline__ void store_staged_chunk(const Params& p, const CUtensorMap* tmap_d,
+                                                   const uint32_t (&packed)[16], uint8_t* buf, int row0, int n,
+                                                   int lane, int chunk_iter) {
     if (lane == ((chunk_iter - 1) & 31)) ptx::bulk_wait_group_read<0>();
     __syncwarp();
     uint8_t* row = buf + 64 * lane;
@@ -976,31 +984,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             ptx::tc_fence_after();
             // Only a later tile of this pair that reuses accumulator b waits for it.
             const bool release = t + C::ACC_BUFS * npairs < p.num_tiles;
-            // The TMEM load of the next chunk is in flight while one is converted and stored.
+            // Chunks go two at a time: both are converted together (independent
+            // work for the warp's latency), then the next two TMEM loads are issued
+            // into the freed registers while the converted pair is stored.
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + b * TW + 32 * h;
             uint32_t ra[32], rb[32];
             ptx::tmem_ld_32x32b_x32(tbase, ra);
+            if (kMyChunks > 1) ptx::tmem_ld_32x32b_x32(tbase + 64, rb);
 #pragma unroll
-            for (int j = 0; j < kMyChunks; ++j) {
-                uint32_t(&r)[32] = (j & 1) ? rb : ra;
-                const int c = h + 2 * j;
+            for (int j = 0; j < kMyChunks; j += 2) {
+                const bool two = j + 1 < kMyChunks;
+                const int c0 = h + 2 * j, c1 = c0 + 2;
+                const bool in0 = n0 + 32 * c0 < p.n_out, in1 = two && n0 + 32 * c1 < p.n_out;
                 ptx::tmem_ld_wait();
-                if (j + 1 < kMyChunks) {
-                    ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 1), (j & 1) ? ra : rb);
-                } else if (release) {
-                    // Every TMEM read of this accumulator is done: hand it back to the MMA issuer.
-                    ptx::tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) ptx::mbar_arrive_cluster(acc_empty0 + (uint32_t)b * 8u);
-                }
-                if (n0 + 32 * c >= p.n_out) continue;
                 if (p.tma_store) {
-                    if (m - lane < p.m) {  // the warp's 32 rows start inside D
-                        stage_chunk_tma(p, &tmap_d, r, wbias + 8 * j, epi, m - lane, n0 + 32 * c, lane, chunk_iter);
-                        ++chunk_iter;
+                    uint32_t pa[16], pb[16];
+                    convert_chunk(p, ra, wbias + 8 * j, pa);
+                    if (two) convert_chunk(p, rb, wbias + 8 * (j + 1), pb);
+                    if (j + 2 < kMyChunks) {
+                        ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 2), ra);
+                        if (j + 3 < kMyChunks) ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 3), rb);
+                    } else if (release) {
+                        // Every TMEM read of this accumulator is done: hand it back to the MMA issuer.
+                        ptx::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) ptx::mbar_arrive_cluster(acc_empty0 + (uint32_t)b * 8u);
                     }
-                } else if (m < p.m) {
-                    store_chunk(p, r, m, n0 + 32 * c);
+                    if (m - lane < p.m) {  // the warp's 32 rows start inside D
+                        if (in0) store_staged_chunk(p, &tmap_d, pa, epi, m - lane, n0 + 32 * c0, lane, chunk_iter++);
+                        if (in1) store_staged_chunk(p, &tmap_d, pb, epi, m - lane, n0 + 32 * c1, lane, chunk_iter++);
+                    }
+                } else {
+                    if (m < p.m) {
+                        if (in0) store_chunk(p, ra, m, n0 + 32 * c0);
+                        if (in1) store_chunk(p, rb, m, n0 + 32 * c1);
+                    }
+                    if (j + 2 < kMyChunks) {
+                        ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 2), ra);
+                        if (j + 3 < kMyChunks) ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 3), rb);
+                    } else if (release) {
+                        ptx::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) ptx::mbar_arrive_cluster(acc_empty0 + (uint32_t)b * 8u);
+                    }
                 }
             }
         }
