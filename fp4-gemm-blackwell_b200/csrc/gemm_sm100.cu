@@ -717,6 +717,35 @@ __device__ __forceinline__ void quantize_phase(const Params& p, const qcore::Sme
     count_tiles(p, lane, counted, p.m_tiles);
 }
 
+// Epilogue of a CTA pair's last tile by a team of warps per TMEM lane
+// quadrant q: the two epilogue warps q and q + 4 (members 0, 1) and the warps
+// whose roles have ended (8 and 12 on quadrant 0, 9, 10, 11 on quadrants 1-3).
+// Member ti of ts takes 32-column chunks c = ti, ti + ts, ...
+// Chunk c's fp32 bias was staged by epilogue warp q + 4 (c & 1) at float4
+// offset 8 (c >> 1).  tq: TMEM address of the quadrant's accumulator; buf: the
+// member's 2 KB staging buffer; m: this lane's output row.
+template <int TW>
+__device__ __forceinline__ void team_epilogue(const Params& p, const CUtensorMap* tmap_d, uint32_t tq,
+                                              const float4* sBias, int q, int ti, int ts, uint8_t* buf,
+                                              int& chunk_iter, int m, int n0, int lane) {
+    constexpr int CH = TW / 32;
+#pragma unroll 1
+    for (int c = ti; c < CH; c += ts) {
+        uint32_t r[32];
+        ptx::tmem_ld_32x32b_x32(tq + 32 * c, r);
+        ptx::tmem_ld_wait();
+        if (n0 + 32 * c >= p.n_out) continue;
+        if (p.tma_store) {
+            uint32_t pk[16];
+            convert_chunk(p, r, sBias + (q + 4 * (c & 1)) * (TW / 8) + 8 * (c >> 1), pk);
+            if (m - lane < p.m)  // the warp's 32 rows start inside D
+                store_staged_chunk(p, tmap_d, pk, buf, m - lane, n0 + 32 * c, lane, chunk_iter++);
+        } else if (m < p.m) {
+            store_chunk(p, r, m, n0 + 32 * c);
+        }
+    }
+}
+
 template <int BN, int STAGES, bool FUSED, int NSUB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     nvf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -739,7 +768,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     uint64_t* acc_full = empty + STAGES;     // [2]
     uint64_t* acc_empty = acc_full + 2;      // [2]
     uint64_t* mma_done = acc_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    uint64_t* bias_ready = mma_done + 1;  // the epilogue warps staged the last tile's bias
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bias_ready + 1);
     int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -760,6 +790,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             ptx::mbar_init(&acc_empty[b], 2 * kPairEpiWarps);
         }
         ptx::mbar_init(mma_done, 1);
+        ptx::mbar_init(bias_ready, kPairEpiWarps);
         *s_abort = 0;
         ptx::fence_mbar_init();
         ptx::prefetch_tmap(&tmap_a);
@@ -967,12 +998,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             const int n0 = n_tile * TW;
             const int m = m_tile * 2 * kBM + (int)rank * kBM + q * 32 + lane;
             const int b = tile_iter % C::ACC_BUFS;
+            const bool last_tile = t + npairs >= p.num_tiles;
             if (p.bias) {
                 __syncwarp();  // the previous tile's reads of wbias are done
 #pragma unroll
                 for (int j = 0; j < kMyChunks; ++j) stage_bias(p, wbias + 8 * j, n0 + 32 * (h + 2 * j), 32, lane);
                 __syncwarp();
             }
+            if (last_tile && lane == 0) ptx::mbar_arrive(bias_ready);
             const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(&acc_full[b], (tile_iter / C::ACC_BUFS) & 1));
             if (!ok || __any_sync(0xffffffffu, aborted(s_abort))) {
                 if (lane == 0 && !ok) {
@@ -982,6 +1015,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 break;
             }
             ptx::tc_fence_after();
+            if (last_tile) {
+                // Shared with the warps whose roles have ended (team_epilogue).
+                if (!__all_sync(0xffffffffu, ptx::mbar_wait(bias_ready, 0))) {
+                    if (lane == 0) {
+                        record_error(p.err, kErrEpilogueTimeout);
+                        atomicExch(s_abort, 1);
+                    }
+                    break;
+                }
+                team_epilogue<TW>(p, &tmap_d, tmem + ((uint32_t)(q * 32) << 16) + b * TW, sBias, q, h,
+                                  q == 0 ? 4 : 3, epi, chunk_iter, m, n0, lane);
+                continue;
+            }
             // Only a later tile of this pair that reuses accumulator b waits for it.
             const bool release = t + C::ACC_BUFS * npairs < p.num_tiles;
             // Chunks go two at a time: both are converted together (independent
@@ -1032,6 +1078,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         }
         ptx::bulk_wait_group_all();  // every lane's stores have read shared memory and written D
         if (p.npeers > 0) __threadfence_system();  // peer stores visible before the kernel ends
+    }
+
+    if (warp >= kPairMmaWarp && !__any_sync(0xffffffffu, aborted(s_abort))) {
+        // -------------------------------------------- MMA and producer warps: help with the last tile
+        const int q = warp & 3;
+        const int ti = warp == kPairThreads / 32 - 1 ? 3 : 2;  // warp 12 is quadrant 0's fourth member
+        const int n_pair = (p.num_tiles - pair + npairs - 1) / npairs;
+        const int t = pair + (n_pair - 1) * npairs;
+        const int last_iter = n_pair - 1;
+        const int b = last_iter % C::ACC_BUFS;
+        int m_tile, n_tile;
+        tile_coords(t, p.m_tiles, p.n_tiles, TILE_M, m_tile, n_tile);
+        const int n0 = n_tile * TW;
+        const int m = m_tile * 2 * kBM + (int)rank * kBM + q * 32 + lane;
+        const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(bias_ready, 0)) &&
+                        __all_sync(0xffffffffu, ptx::mbar_wait(&acc_full[b], (last_iter / C::ACC_BUFS) & 1));
+        if (!ok) {
+            if (lane == 0) {
+                record_error(p.err, kErrEpilogueTimeout);
+                atomicExch(s_abort, 1);
+            }
+        } else if (!__any_sync(0xffffffffu, aborted(s_abort))) {
+            ptx::tc_fence_after();
+            // Every MMA has completed and no load is left: the operand ring is idle.
+            int chunk_iter = 0;
+            team_epilogue<TW>(p, &tmap_d, tmem + ((uint32_t)(q * 32) << 16) + b * TW, sBias, q, ti, q == 0 ? 4 : 3,
+                              smem + (warp - kPairMmaWarp) * 2048, chunk_iter, m, n0, lane);
+            ptx::bulk_wait_group_all();
+            if (p.npeers > 0) __threadfence_system();
+        }
     }
 
     ptx::tc_fence_before();
