@@ -100,22 +100,27 @@ __global__ void __launch_bounds__(kThreads, 6) nvfp4_quantize_kernel(const __gri
 
 // Staged variant for dense inputs (rows stored back to back, ld == cols ==
 // padded K, 16-byte aligned): the blocks of rows [0, rows) are one contiguous
-// array of 32-byte blocks, so span j (blocks 256j .. 256j + 255, 8 KB) is one
-// 1-D bulk copy.  A producer warp streams the spans of this CTA (j = CTA,
-// CTA + G, ...) into a ring of shared-memory stages with cp.async.bulk;
-// eight consumer warps quantize one block per thread from shared memory and
-// release the stage.  Five CTAs per SM keep 160 KB of input in flight per SM
-// with no registers spent on it.  Blocks of the padding rows are zeros.
+// array of 32-byte blocks, so span j (BPC x 256 blocks) is one 1-D bulk copy.
+// A producer warp streams the spans of this CTA (j = CTA, CTA + G, ...) into a
+// ring of STAGES shared-memory stages with cp.async.bulk; eight consumer warps
+// quantize BPC blocks per thread from shared memory and release the stage.
+// BPC = 1: 8 KB spans, 4 stages, 5 CTAs per SM (160 KB in flight per SM);
+// BPC = 2: 16 KB spans, 2 stages, 4 CTAs per SM (128 KB in flight), which
+// halves the per-span work (barriers, index arithmetic) per block but leaves
+// fewer spans per CTA, so it is used from 4 Mi blocks up.  Blocks of the
+// padding rows are zeros.
 constexpr int kStagedWarps = 8;
 constexpr int kStagedThreads = (kStagedWarps + 1) * 32;
-constexpr int kSpanBlocks = kStagedWarps * 32;
-constexpr int kSpanBytes = kSpanBlocks * 32;
-constexpr int kStagedStages = 4;
 constexpr int kErrQuantStageTimeout = 5;  // device error word: a quantizer ring wait gave up
 constexpr uint64_t kQuantDrainNs = 200000;  // after a timeout, let issued copies land
+constexpr uint32_t kTwoBlocksFrom = 1u << 22;  // blocks of a launch from which BPC = 2
 
-__global__ void __launch_bounds__(kStagedThreads, 5)
+template <int BPC, int STAGES, int MIN_CTAS>
+__global__ void __launch_bounds__(kStagedThreads, MIN_CTAS)
     nvfp4_quantize_staged_kernel(const __grid_constant__ QuantParams p, int* err) {
+    constexpr int kSpanBlocks = kStagedWarps * 32 * BPC;
+    constexpr int kSpanBytes = kSpanBlocks * 32;
+    constexpr int kStagedStages = STAGES;
     __shared__ __align__(128) uint8_t s_stage[kStagedStages][kSpanBytes];
     __shared__ __align__(16) uint8_t s_tables[kSmemTableBytes];
     __shared__ __align__(8) uint64_t full[kStagedStages], empty[kStagedStages];
@@ -171,20 +176,25 @@ __global__ void __launch_bounds__(kStagedThreads, 5)
                 timed_out = !ok;
                 break;
             }
-            const uint32_t idx = span * kSpanBlocks + threadIdx.x;
-            const uint32_t r = (__umulhi(idx, p.div_mul) + idx) >> p.div_shift;
-            const uint32_t kb = idx - r * p.nsb;
-            uint32_t w[8];
-            if (idx < dense) {
-                const uint4* src = reinterpret_cast<const uint4*>(s_stage[s] + threadIdx.x * 32u);
-                const uint4 v0 = src[0], v1 = src[1];
-                w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
-                w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
-            } else {
+            uint32_t w[BPC][8], idx[BPC], r[BPC], kb[BPC];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) w[i] = 0u;
+            for (int u = 0; u < BPC; ++u) {
+                const uint32_t off = threadIdx.x + (uint32_t)u * (kStagedWarps * 32);
+                idx[u] = span * kSpanBlocks + off;
+                r[u] = (__umulhi(idx[u], p.div_mul) + idx[u]) >> p.div_shift;
+                kb[u] = idx[u] - r[u] * p.nsb;
+                if (idx[u] < dense) {
+                    const uint4* src = reinterpret_cast<const uint4*>(s_stage[s] + off * 32u);
+                    const uint4 v0 = src[0], v1 = src[1];
+                    w[u][0] = v0.x; w[u][1] = v0.y; w[u][2] = v0.z; w[u][3] = v0.w;
+                    w[u][4] = v1.x; w[u][5] = v1.y; w[u][6] = v1.z; w[u][7] = v1.w;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) w[u][i] = 0u;
+                }
             }
-            quantize_and_store(p, idx, p.total, w, r, kb, lane, tab);
+#pragma unroll
+            for (int u = 0; u < BPC; ++u) quantize_and_store(p, idx[u], p.total, w[u], r[u], kb[u], lane, tab);
             // The stage's bytes were consumed above (the stores depend on them).
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&empty[s]);
@@ -293,11 +303,21 @@ cudaError_t quantize_launch(const QuantizeArgs& a, cudaStream_t stream) {
     const char* staged_env = getenv("FP4B_QUANT_STAGED");
     const bool staged_ok = staged_env ? atoi(staged_env) != 0 : true;
     if (staged_ok && p.vec_ok && p.ld == p.cols && p.cols == p.nsb * kSfVec) {
+        if (p.total >= kTwoBlocksFrom) {
+            auto kernel = nvfp4_quantize_staged_kernel<2, 2, 4>;
+            static std::once_flag once[64];
+            static int cache[64];
+            const uint64_t need = ((uint64_t)p.total + 511) / 512;
+            const uint64_t cap = (uint64_t)resident_ctas(kernel, kStagedThreads, once, cache);
+            return launch_pdl(kernel, (uint32_t)(need < cap ? need : cap), kStagedThreads, stream, p,
+                              device_error_word());
+        }
+        auto kernel = nvfp4_quantize_staged_kernel<1, 4, 5>;
         static std::once_flag once[64];
         static int cache[64];
-        const uint64_t need = ((uint64_t)p.total + kSpanBlocks - 1) / kSpanBlocks;
-        const uint64_t cap = (uint64_t)resident_ctas(nvfp4_quantize_staged_kernel, kStagedThreads, once, cache);
-        return launch_pdl(nvfp4_quantize_staged_kernel, (uint32_t)(need < cap ? need : cap), kStagedThreads, stream, p,
+        const uint64_t need = ((uint64_t)p.total + 255) / 256;
+        const uint64_t cap = (uint64_t)resident_ctas(kernel, kStagedThreads, once, cache);
+        return launch_pdl(kernel, (uint32_t)(need < cap ? need : cap), kStagedThreads, stream, p,
                           device_error_word());
     }
     static std::once_flag once[64];
