@@ -568,11 +568,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ CTA-pair kernel
-// 256 x BN output tiles on a cluster of two CTAs with tcgen05 cta_group::2:
-// CTA r of the pair loads rows [128r, 128r + 128) of the A tile, rows
-// [r*BN/2, (r+1)*BN/2) of the B tile, the scale atoms of its own A rows and
-// the scale atoms of all BN B rows; the even CTA issues one M=256 MMA per
-// 64-wide k-block for both.  Per SM this moves a third less operand data per
+// 256 x BN output tiles (or 256 x 2BN, see PairCfg) on a cluster of two CTAs
+// with tcgen05 cta_group::2: CTA r of the pair loads rows [128r, 128r + 128)
+// of the A tile, rows [r*BN/2, (r+1)*BN/2) of the B tile, the scale atoms of
+// its own A rows and the scale atoms of all B rows of the tile; the even CTA
+// issues one M=256 MMA per 64-wide k-block (and N-subtile) for both.  Per SM this moves a third less operand data per
 // FLOP than a 128 x BN tile on one SM, and halves the MMA instructions.
 //
 // Synchronisation across the pair:
@@ -581,15 +581,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 //                producer posts the expected bytes of both.
 //   empty[s]     in both CTAs: CTA 0's commit arrives on both.
 //   acc_full[b]  in both CTAs: CTA 0's commit arrives on both.
-//   acc_empty[b] in CTA 0: the epilogue warps of both CTAs arrive (8 arrivals).
+//   acc_empty[b] in CTA 0: the 8 epilogue warps of both CTAs arrive (16 arrivals).
 //   mma_done     in both CTAs: the last commit; every MMA of the pair is done.
+//   bias_ready   in each CTA: its 8 epilogue warps staged the last tile's bias,
+//                which the whole team of the last tile reads.
 // Scale-factor boxes are loaded with 3-D tensor maps over the atom array
 // ([row tile][k-block][512 bytes]) so they too can complete on CTA 0's barrier.
 //
 // 416 threads: warps 0-7 epilogue (warp w reads TMEM lanes 32(w%4)..+31 and
 // stores the 32-column chunks c with c % 2 == w / 4), warp 8 TMEM allocation
 // and MMA issue, warps 9-12 one producer per copy type
-// (A, B, scale-A, scale-B).  A TMA issue keeps its warp busy for ~130 ns on
+// (A, B, scale-A, scale-B).  The pair's last tile is stored by all 13 warps
+// (team_epilogue): the MMA and producer warps have nothing left to do.  A TMA issue keeps its warp busy for ~130 ns on
 // B200 and one thread's copies run one after another (~0.4 us each), so the
 // four copies of a stage go out from four warps in parallel, each from a lane
 // that has not issued for 32 stages.
