@@ -98,9 +98,12 @@ __global__ void __launch_bounds__(kThreads, 6) nvfp4_quantize_kernel(const __gri
     }
 }
 
-// Staged variant for dense inputs (rows stored back to back, ld == cols ==
-// padded K, 16-byte aligned): the blocks of rows [0, rows) are one contiguous
-// array of 32-byte blocks, so span j (BPC x 256 blocks) is one 1-D bulk copy.
+// Staged variant for inputs whose rows are stored back to back (ld == cols, a
+// multiple of 64, 16-byte aligned): the stored blocks of rows [0, rows) are one
+// contiguous array of 32-byte blocks, so span j (BPC x 256 of them) is one 1-D
+// bulk copy; a stored block (r, kb) goes to block kb of padded row r.  The
+// blocks that are not stored (the K padding of each row, when cols < K_pad,
+// and the padding rows) are zeros, written after the spans.
 // A producer warp streams the spans of this CTA (j = CTA, CTA + G, ...) into a
 // ring of STAGES shared-memory stages with cp.async.bulk; eight consumer warps
 // quantize BPC blocks per thread from shared memory and release the stage.
@@ -127,8 +130,8 @@ __global__ void __launch_bounds__(kStagedThreads, MIN_CTAS)
     __shared__ int s_abort;
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t nspans = (p.total + kSpanBlocks - 1) / kSpanBlocks;
-    const uint32_t dense = p.rows * p.nsb;  // blocks stored in memory
+    const uint32_t dense = p.rows * p.cpb;  // blocks stored in memory
+    const uint32_t nspans = (dense + kSpanBlocks - 1) / kSpanBlocks;
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStagedStages; ++i) {
             ptx::mbar_init(&full[i], 1);
@@ -176,14 +179,16 @@ __global__ void __launch_bounds__(kStagedThreads, MIN_CTAS)
                 timed_out = !ok;
                 break;
             }
-            uint32_t w[BPC][8], idx[BPC], r[BPC], kb[BPC];
+            uint32_t w[BPC][8], idx[BPC], r[BPC], kb[BPC], end[BPC];
 #pragma unroll
             for (int u = 0; u < BPC; ++u) {
                 const uint32_t off = threadIdx.x + (uint32_t)u * (kStagedWarps * 32);
-                idx[u] = span * kSpanBlocks + off;
-                r[u] = (__umulhi(idx[u], p.div_mul) + idx[u]) >> p.div_shift;
-                kb[u] = idx[u] - r[u] * p.nsb;
-                if (idx[u] < dense) {
+                const uint32_t mb = span * kSpanBlocks + off;  // stored block
+                r[u] = (__umulhi(mb, p.cpb_mul) + mb) >> p.cpb_shift;
+                kb[u] = mb - r[u] * p.cpb;
+                idx[u] = r[u] * p.nsb + kb[u];
+                end[u] = mb < dense ? p.total : 0u;
+                if (mb < dense) {
                     const uint4* src = reinterpret_cast<const uint4*>(s_stage[s] + off * 32u);
                     const uint4 v0 = src[0], v1 = src[1];
                     w[u][0] = v0.x; w[u][1] = v0.y; w[u][2] = v0.z; w[u][3] = v0.w;
@@ -194,10 +199,32 @@ __global__ void __launch_bounds__(kStagedThreads, MIN_CTAS)
                 }
             }
 #pragma unroll
-            for (int u = 0; u < BPC; ++u) quantize_and_store(p, idx[u], p.total, w[u], r[u], kb[u], lane, tab);
+            for (int u = 0; u < BPC; ++u) quantize_and_store(p, idx[u], end[u], w[u], r[u], kb[u], lane, tab);
             // The stage's bytes were consumed above (the stores depend on them).
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&empty[s]);
+        }
+        // Blocks not stored in memory: the K padding of rows [0, rows), then the
+        // padding rows; zeros (code 0, scale 0x01).  Warp-uniform trips; four
+        // consecutive lanes hold four consecutive blocks of one row (the K
+        // padding and K_pad / 16 are multiples of 4).
+        const uint32_t kpad = p.nsb - p.cpb;
+        const uint32_t n_kpad = p.rows * kpad;
+        const uint32_t n_pad = n_kpad + (p.total - p.rows * p.nsb);
+        const uint32_t zero[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+        for (uint32_t i0 = (blockIdx.x * kStagedWarps + warp) * 32u; i0 < n_pad && !timed_out;
+             i0 += gridDim.x * kStagedWarps * 32u) {
+            const uint32_t i = i0 + lane;
+            uint32_t r, kb;
+            if (i < n_kpad) {
+                r = i / kpad;
+                kb = p.cpb + (i - r * kpad);
+            } else {
+                const uint32_t j = i - n_kpad;
+                r = p.rows + j / p.nsb;
+                kb = j - (r - p.rows) * p.nsb;
+            }
+            quantize_and_store(p, r * p.nsb + kb, i < n_pad ? p.total : 0u, zero, r, kb, lane, tab);
         }
     }
     if (timed_out) {
@@ -255,6 +282,8 @@ qcore::QuantParams make_quant_params(const QuantizeArgs& a) {
     p.total = (uint32_t)(a.rows_pad * p.nsb);
     qcore::make_fast_div(p.nsb, &p.div_mul, &p.div_shift);
     p.vec_ok = ((reinterpret_cast<uintptr_t>(a.src) & 15) == 0 && (a.ld % 8) == 0) ? 1u : 0u;
+    p.cpb = (uint32_t)(a.cols / kSfVec);
+    qcore::make_fast_div(p.cpb > 0 ? p.cpb : 1u, &p.cpb_mul, &p.cpb_shift);
     return p;
 }
 
@@ -302,7 +331,7 @@ cudaError_t quantize_launch(const QuantizeArgs& a, cudaStream_t stream) {
     // Dense input: rows back to back with no column padding -> staged kernel.
     const char* staged_env = getenv("FP4B_QUANT_STAGED");
     const bool staged_ok = staged_env ? atoi(staged_env) != 0 : true;
-    if (staged_ok && p.vec_ok && p.ld == p.cols && p.cols == p.nsb * kSfVec) {
+    if (staged_ok && p.vec_ok && p.ld == p.cols && p.cols % 64 == 0) {
         if (p.total >= kTwoBlocksFrom) {
             auto kernel = nvfp4_quantize_staged_kernel<2, 2, 4>;
             static std::once_flag once[64];

@@ -33,6 +33,9 @@ struct QuantParams {
     uint32_t div_mul;  // fast division by nsb: q = (umulhi(n, div_mul) + n) >> div_shift
     uint32_t div_shift;
     uint32_t vec_ok;   // 16-byte aligned rows
+    // Stored blocks of a row (cols / 16 when cols % 16 == 0) with fast division,
+    // for the staged kernel, whose spans walk the rows' stored blocks.
+    uint32_t cpb, cpb_mul, cpb_shift;
 };
 
 // Shared-memory copies of the tables (copy_tables fills them).
