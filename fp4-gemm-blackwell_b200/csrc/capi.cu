@@ -9,6 +9,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -56,6 +57,9 @@ struct WeightCache {
     int N, K;
     int device;
     bool owns;
+    // The cached bytes are of weight * (1 / w_alpha); every GEMM with this cache
+    // multiplies its alpha by w_alpha (1 unless a global weight scale was set).
+    float w_alpha;
 };
 
 __device__ int g_device_error;
@@ -204,7 +208,7 @@ int read_and_clear_device_error() {
 bool cache_view(const void* handle, CacheView* out) {
     WeightCache* c = as_cache(handle);
     if (!c) return false;
-    *out = CacheView{c->fp4, c->sf, c->N, c->K};
+    *out = CacheView{c->fp4, c->sf, c->N, c->K, c->w_alpha};
     return true;
 }
 
@@ -268,7 +272,7 @@ FP4B_EXPORT void* fp4b_quantize_weights_ex(const void* w, int n, int k, int ldw,
         return nullptr;
     }
     const long N = round_up(n, 128), K = round_up(k, 128);
-    auto* c = new WeightCache{kCacheMagic, nullptr, nullptr, (int)N, (int)K, current_device(), true};
+    auto* c = new WeightCache{kCacheMagic, nullptr, nullptr, (int)N, (int)K, current_device(), true, 1.0f};
     void* p = nullptr;
     if (cudaMalloc(&p, (size_t)N * K / 2) != cudaSuccess) {
         cudaGetLastError();
@@ -354,8 +358,8 @@ FP4B_EXPORT int fp4b_run_cached_ex(const void* A, int m, int k_in, int lda, cons
     DeviceState& s = g_state[current_device()];
     if (!reserve(s.a_fp4, (size_t)m_pad * c->K / 2) || !reserve(s.a_sf, (size_t)m_pad * c->K / 16)) return -1;
     cudaStream_t st = as_stream(stream);
-    GemmArgs g{s.a_fp4.ptr, s.a_sf.ptr, c->fp4, c->sf, m, n_out, c->K, m_pad, c->N, C, ldc, D, ldd, bias, alpha,
-               beta};
+    GemmArgs g{s.a_fp4.ptr, s.a_sf.ptr, c->fp4, c->sf, m, n_out, c->K, m_pad, c->N, C, ldc, D, ldd, bias,
+               alpha * c->w_alpha, beta};
     QuantizeArgs q{A, m, k_in, lda, m_pad, c->K, s.a_fp4.ptr, s.a_sf.ptr};
     if (m > 128 && !quantize_check(q) && !gemm_check(g) &&
         reserve_zeroed(s.sync, (size_t)(1 + (m_pad + 255) / 256) * sizeof(uint32_t))) {
@@ -385,8 +389,8 @@ FP4B_EXPORT int fp4b_run_cached_peers(const void* A, int m, int k_in, int lda, c
     DeviceState& s = g_state[current_device()];
     if (!reserve(s.a_fp4, (size_t)m_pad * c->K / 2) || !reserve(s.a_sf, (size_t)m_pad * c->K / 16)) return -1;
     cudaStream_t st = as_stream(stream);
-    GemmArgs g{s.a_fp4.ptr, s.a_sf.ptr, c->fp4, c->sf, m, n_out, c->K, m_pad, c->N, nullptr, 0, D, ldd, bias, 1.0f,
-               0.0f};
+    GemmArgs g{s.a_fp4.ptr, s.a_sf.ptr, c->fp4, c->sf, m, n_out, c->K, m_pad, c->N, nullptr, 0, D, ldd, bias,
+               c->w_alpha, 0.0f};
     if (const char* why = gemm_check(g)) {
         set_last_error("gemm: %s", why);
         return -2;
@@ -543,7 +547,22 @@ FP4B_EXPORT void* fp4b_weight_cache_slice(const void* h, int row0, int rows) {
         return nullptr;
     }
     return new WeightCache{kCacheMagic, c->fp4 + (size_t)row0 * c->K / 2, c->sf + (size_t)row0 * c->K / 16, rows,
-                           c->K, c->device, false};
+                           c->K, c->device, false, c->w_alpha};
+}
+
+FP4B_EXPORT int fp4b_weight_cache_set_alpha(void* h, float w_alpha) {
+    WeightCache* c = as_cache(h);
+    if (!c || !(w_alpha > 0.0f) || !std::isfinite(w_alpha)) {
+        set_last_error("fp4b_weight_cache_set_alpha: null handle or non-positive / non-finite factor");
+        return -1;
+    }
+    c->w_alpha = w_alpha;
+    return 0;
+}
+
+FP4B_EXPORT float fp4b_weight_cache_alpha(const void* h) {
+    WeightCache* c = as_cache(h);
+    return c ? c->w_alpha : 0.0f;
 }
 
 FP4B_EXPORT int fp4b_weight_cache_export(const void* h, void* dst_fp4, void* dst_sf, void* stream) {
@@ -582,5 +601,5 @@ FP4B_EXPORT void* fp4b_weight_cache_import(const void* src_fp4, const void* src_
         return nullptr;
     }
     return new WeightCache{kCacheMagic, static_cast<uint8_t*>(a), static_cast<uint8_t*>(b), N, K, current_device(),
-                           true};
+                           true, 1.0f};
 }

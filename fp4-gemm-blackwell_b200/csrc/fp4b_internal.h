@@ -65,6 +65,7 @@ struct CacheView {
     const uint8_t* fp4;
     const uint8_t* sf;
     int N, K;
+    float w_alpha;  // factor every GEMM with the cache applies (global weight scale)
 };
 // False for a null or foreign handle.
 bool cache_view(const void* handle, CacheView* out);

@@ -110,7 +110,7 @@ FP4B_EXPORT int fp4b_run_cached_noalloc(const void* A, int m, int k_in, int lda,
         set_last_error("fp4b_run_cached_noalloc: quantize launch: %s", cudaGetErrorString(e));
         return -4;
     }
-    GemmArgs g{a_fp4, a_sf, c.fp4, c.sf, m, n_out, c.K, m_pad, c.N, C, ldc, D, ldd, bias, alpha, beta};
+    GemmArgs g{a_fp4, a_sf, c.fp4, c.sf, m, n_out, c.K, m_pad, c.N, C, ldc, D, ldd, bias, alpha * c.w_alpha, beta};
     if (const char* why = gemm_check(g)) {
         set_last_error("fp4b_run_cached_noalloc: %s", why);
         return -1;

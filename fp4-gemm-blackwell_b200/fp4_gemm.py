@@ -26,6 +26,7 @@ There is no fallback: importing this module fails if the library is missing.
 """
 
 import ctypes
+import math
 import os
 
 import torch
@@ -70,6 +71,8 @@ _bind("fp4b_run_cached_ex", _i, [_vp, _i, _i, _i, _vp, _i, _vp, _i, _vp, _i, _vp
 _bind("fp4b_run_ex", _i, [_vp, _i, _i, _i, _vp, _i, _i, _vp, _i, _vp, _i, _vp, _f, _f, _vp])
 _bind("fp4b_quantize_weights_ex", _vp, [_vp, _i, _i, _i, _vp, _i])
 _bind("fp4b_weight_cache_slice", _vp, [_vp, _i, _i])
+_bind("fp4b_weight_cache_set_alpha", _i, [_vp, _f])
+_bind("fp4b_weight_cache_alpha", _f, [_vp])
 _bind("fp4b_weight_cache_export", _i, [_vp, _vp, _vp, _vp])
 _bind("fp4b_weight_cache_import", _vp, [_vp, _vp, _i, _i, _vp])
 _bind("fp4b_run_cached_peers", _i, [_vp, _i, _i, _i, _vp, _i, _vp, _i, ctypes.POINTER(_vp), _i, _vp, _vp])
@@ -89,6 +92,22 @@ def _chunk_schedule(m: int, chunk_rows: int) -> list:
     with PCIe Gen5 a tail of halving chunks (512, 256, 128, ...) measured slower
     than equal 512-row chunks, whose copies already hide the per-chunk GEMMs."""
     return [min(chunk_rows, m - r) for r in range(0, m, chunk_rows)]
+
+
+# Largest UE4M3 block scale the quantizer produces (the clamp of fp4_gemm_lib.cu:128-164).
+_UE4M3_MAX = 480.0
+
+
+def global_weight_scale(amax: float) -> float:
+    """Power of two s for two-level NVFP4 weights: quantizing weight * s puts the
+    largest block scale (|w|max * s / 6) at or just below the UE4M3 maximum 480,
+    so that the block scales of small-magnitude weights use UE4M3's normal range
+    (rounded) instead of its subnormals (truncated).  A power of two keeps
+    weight * s exact in BF16 and 1 / s exact in the GEMM's alpha.  1 for a zero
+    or non-finite |w|max."""
+    if not (amax > 0.0) or amax != amax or amax == float("inf"):
+        return 1.0
+    return 2.0 ** math.floor(math.log2(6.0 * _UE4M3_MAX / amax))
 
 
 def _pad_to_multiple(x: int, m: int) -> int:
@@ -260,13 +279,19 @@ class FP4WeightCache:
     reference's cache for the same weight.
     """
 
-    def __init__(self, weight: torch.Tensor, bias: torch.Tensor = None):
+    def __init__(self, weight: torch.Tensor, bias: torch.Tensor = None, global_scale: bool = False):
         """
         Quantize a weight matrix to FP4 and cache on device.
 
         Args:
             weight: [N, K] BF16 weight matrix on CUDA
             bias: Optional [N] bias vector
+            global_scale: two-level NVFP4 (not in the reference; off by default,
+                which keeps the reference's bytes): cache weight * s with the
+                power of two s of ``global_weight_scale(|weight|max)``, and
+                multiply every GEMM with the cache by 1 / s.  Improves the
+                accuracy of small-magnitude weights (e.g. N(0, 0.02)), whose
+                block scales otherwise fall in UE4M3's truncated subnormals.
         """
         self._handle = None
         assert weight.dim() == 2, f"Weight must be 2D [N, K], got {weight.shape}"
@@ -283,6 +308,11 @@ class FP4WeightCache:
 
         if weight.dtype != torch.bfloat16:
             weight = weight.to(torch.bfloat16)
+        self.global_scale = 1.0
+        if global_scale:
+            self.global_scale = global_weight_scale(float(weight.abs().max().float()))
+            if self.global_scale != 1.0:
+                weight = (weight.float() * self.global_scale).to(torch.bfloat16)  # exact: a power of two
         weight, ldw = _rows_view(weight)
         self.device = weight.device
 
@@ -292,6 +322,8 @@ class FP4WeightCache:
         if not handle:
             raise RuntimeError("fp4_quantize_weights failed")
         self._handle = handle
+        if self.global_scale != 1.0 and _lib.fp4b_weight_cache_set_alpha(handle, 1.0 / self.global_scale) != 0:
+            raise RuntimeError(f"fp4b_weight_cache_set_alpha failed ({_last_error()})")
 
         # Memory tracking
         self.fp4_bytes = self.N * self.K // 2
@@ -307,6 +339,8 @@ class FP4WeightCache:
         obj.K = _lib.fp4_weight_cache_K(handle)
         obj.padded = (obj.N != n_orig or obj.K != k_orig)
         obj.device = device
+        w_alpha = _lib.fp4b_weight_cache_alpha(handle)
+        obj.global_scale = 1.0 / w_alpha if w_alpha > 0 else 1.0
         obj.fp4_bytes = obj.N * obj.K // 2
         obj.sf_bytes = obj.N * (obj.K // 16)
         return obj
@@ -481,7 +515,8 @@ class FP4WeightCache:
             rc = _lib.fp4b_weight_cache_export(self._handle, fp4.data_ptr(), sf.data_ptr(), _stream_ptr(self.device))
         if rc != 0:
             raise RuntimeError(f"fp4b_weight_cache_export failed ({_last_error()})")
-        return {"fp4": fp4, "sf": sf, "N_orig": self.N_orig, "K_orig": self.K_orig, "bias": self.bias}
+        return {"fp4": fp4, "sf": sf, "N_orig": self.N_orig, "K_orig": self.K_orig, "bias": self.bias,
+                "global_scale": self.global_scale}
 
     @classmethod
     def from_state_dict(cls, sd: dict, device=None) -> "FP4WeightCache":
@@ -496,6 +531,10 @@ class FP4WeightCache:
             h = _lib.fp4b_weight_cache_import(fp4.data_ptr(), sf.data_ptr(), n, k, _stream_ptr(device))
         if not h:
             raise RuntimeError(f"fp4b_weight_cache_import failed ({_last_error()})")
+        g = float(sd.get("global_scale", 1.0))
+        if g != 1.0 and _lib.fp4b_weight_cache_set_alpha(h, 1.0 / g) != 0:
+            _lib.fp4_weight_cache_free(ctypes.c_void_p(h))
+            raise RuntimeError(f"fp4b_weight_cache_set_alpha failed ({_last_error()})")
         bias = sd.get("bias")
         if bias is not None:
             bias = bias.to(device)
@@ -523,18 +562,19 @@ class FP4WeightCache:
         return f"FP4WeightCache([{self.N_orig}, {self.K_orig}], {mb:.1f} MB, {status})"
 
 
-def fp4_quantize(weight: torch.Tensor, bias: torch.Tensor = None) -> FP4WeightCache:
+def fp4_quantize(weight: torch.Tensor, bias: torch.Tensor = None, global_scale: bool = False) -> FP4WeightCache:
     """
     Quantize a weight matrix to FP4 and cache on device.
 
     Args:
         weight: [N, K] BF16 weight matrix on CUDA
         bias: Optional [N] bias vector
+        global_scale: opt-in two-level NVFP4 (see FP4WeightCache)
 
     Returns:
         FP4WeightCache handle for fast inference
     """
-    return FP4WeightCache(weight, bias)
+    return FP4WeightCache(weight, bias, global_scale=global_scale)
 
 
 def fp4_cached_matmul(

@@ -147,6 +147,15 @@ void* fp4b_quantize_weights_ex(const void* weight_bf16, int n, int k, int ldw, v
  * NULL on failure. */
 void* fp4b_weight_cache_slice(const void* cache_handle, int row0, int rows);
 
+/* Global weight scale (two-level NVFP4; no counterpart in the reference): a
+ * cache built from weight * s instead of weight carries w_alpha = 1 / s, and
+ * every GEMM with it (fp4_gemm_run_cached and the fp4b_run_cached_* entry
+ * points) multiplies its alpha by w_alpha.  Caches start at 1 (the reference's
+ * bytes); slices inherit their parent's factor.  set: 0, or -1 for a bad
+ * handle or a factor that is not positive and finite.  get: 0 for a bad handle. */
+int fp4b_weight_cache_set_alpha(void* cache_handle, float w_alpha);
+float fp4b_weight_cache_alpha(const void* cache_handle);
+
 /* Copy a cache's bytes (packed E2M1 N*K/2, then scales N*K/16; N, K from the
  * getters) into caller device buffers, asynchronously on `stream`: the payload
  * of a serialised weight cache.  0 ok, -1 bad arguments, -4 copy failure. */

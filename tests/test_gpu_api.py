@@ -223,3 +223,65 @@ def test_fused_quantize_gemm_equals_two_kernels(cuda, fp4, monkeypatch, m, n, k)
             assert torch.equal(f, two)
         assert fp4.device_error() == 0
     assert_gemm_close(two, oracle_linear(x, w, bias=b), f"fused {m}x{n}x{k}")
+
+
+def test_global_scale_cache(cuda, fp4):
+    # Opt-in two-level NVFP4 for N(0, 0.02) weights: the cache holds weight * s
+    # (s a power of two) and every GEMM with it applies 1 / s.  Pearson with the
+    # unquantized fp32 product reaches 0.99 (0.988 with the reference's
+    # one-level scales); the result is the oracle GEMM of the scaled weight
+    # times 1 / s; the factor survives state_dict and shards.
+    from tests.gpu_helpers import pearson
+    m, n, k = 512, 640, 1024
+    x, w, b = W.cached_linear_inputs(m, n, k, seed=31)
+    xd, wd, bd = x.to(cuda), w.to(cuda), b.to(cuda)
+    ref32 = x.float() @ w.float().t() + b.float()
+    with fp4.FP4WeightCache(wd, bd) as plain, fp4.FP4WeightCache(wd, bd, global_scale=True) as scaled:
+        s = scaled.global_scale
+        assert s == fp4.global_weight_scale(float(w.abs().max())) and s > 1.0
+        assert plain.global_scale == 1.0
+        y0, y1 = plain.forward(xd), scaled.forward(xd)
+        p0, p1 = pearson(y0, ref32), pearson(y1, ref32)
+        assert p1 >= 0.99 and p1 > p0, (p0, p1)
+        ws = (w.float() * s).to(torch.bfloat16)
+        assert_gemm_close(y1, oracle_linear(x, ws, bias=b, alpha=1.0 / s), "global scale")
+        sd = {key: (v.cpu() if torch.is_tensor(v) else v) for key, v in scaled.state_dict().items()}
+        assert sd["global_scale"] == s
+        c2 = fp4.FP4WeightCache.from_state_dict(sd, device=cuda)
+        assert c2.global_scale == s
+        assert torch.equal(c2.forward(xd), y1)
+        c2.free()
+        part = scaled.shard(128, 256, bias=bd[128:384])
+        assert part.global_scale == s
+        assert torch.equal(part.forward(xd), y1[:, 128:384])
+        part.free()
+
+
+def test_cuda_graph_capture_of_cached_linears(cuda, fp4):
+    # Stream-ordered back-to-back cached linears (no per-call sync) captured in
+    # a CUDA graph replay to the eager bytes, also after new input data is
+    # copied into the captured input buffer.
+    x, w1, b1 = W.cached_linear_inputs(512, 640, 1024, seed=41)
+    _, w2, b2 = W.cached_linear_inputs(512, 384, 640, seed=43)
+    with fp4.FP4WeightCache(w1.to(cuda), b1.to(cuda)) as l1, fp4.FP4WeightCache(w2.to(cuda), b2.to(cuda)) as l2:
+        xd = x.to(cuda)
+        eager = l2.forward(l1.forward(xd, sync=False), sync=False)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):  # warm-up outside the capture (scratch allocated)
+            for _ in range(2):
+                l2.forward(l1.forward(xd, sync=False), sync=False)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = l2.forward(l1.forward(xd, sync=False), sync=False)
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
+        x2, _, _ = W.cached_linear_inputs(512, 640, 1024, seed=45)
+        xd.copy_(x2.to(cuda))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, l2.forward(l1.forward(xd)))
+        assert fp4.device_error() == 0
+        del graph
