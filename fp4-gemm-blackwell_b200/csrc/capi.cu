@@ -368,6 +368,7 @@ FP4B_EXPORT int fp4b_run_cached_ex(const void* A, int m, int k_in, int lda, cons
         if (e != cudaErrorNotSupported) return launch_status(e, "fused quantize+gemm launch");
     }
     if (int rc = quantize_into(A, m, k_in, lda, s.a_fp4.ptr, s.a_sf.ptr, m_pad, c->K, st)) return rc;
+    g.b_cached = true;
     return gemm_into(g, st);
 }
 
@@ -396,6 +397,7 @@ FP4B_EXPORT int fp4b_run_cached_peers(const void* A, int m, int k_in, int lda, c
         return -2;
     }
     if (int rc = quantize_into(A, m, k_in, lda, s.a_fp4.ptr, s.a_sf.ptr, m_pad, c->K, st)) return rc;
+    g.b_cached = true;
     const cudaError_t e = gemm_launch_peers(g, peer_d, npeers, st);
     if (e == cudaErrorNotSupported) {
         set_last_error("fp4b_run_cached_peers: needs 16-byte aligned output rows");

@@ -38,6 +38,12 @@ struct GemmArgs {
     long ldd;
     const void* bias;  // bf16 [n_out] or null
     float alpha, beta;
+    // B is a weight cache and the GEMM is launched right behind the activation
+    // quantizer on the same stream.  That quantizer lets the GEMM launch only
+    // after its own programmatic wait, i.e. after every earlier kernel
+    // (including one that wrote the cache) completed, so the CTA-pair kernel
+    // may load B before its own programmatic wait.
+    bool b_cached = false;
 };
 
 const char* gemm_check(const GemmArgs& g);

@@ -115,6 +115,7 @@ FP4B_EXPORT int fp4b_run_cached_noalloc(const void* A, int m, int k_in, int lda,
         set_last_error("fp4b_run_cached_noalloc: %s", why);
         return -1;
     }
+    g.b_cached = true;  // right behind the activation quantizer
     e = gemm_launch(g, st);
     if (e != cudaSuccess) {
         set_last_error("fp4b_run_cached_noalloc: gemm launch: %s", cudaGetErrorString(e));

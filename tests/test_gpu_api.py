@@ -225,6 +225,54 @@ def test_fused_quantize_gemm_equals_two_kernels(cuda, fp4, monkeypatch, m, n, k)
     assert_gemm_close(two, oracle_linear(x, w, bias=b), f"fused {m}x{n}x{k}")
 
 
+@pytest.mark.parametrize("m,n,k,bn", [(2048, 2880, 7680, None), (4096, 5760, 2880, "256"), (384, 1000, 640, "128"),
+                                      (2304, 3200, 1024, "384")])
+def test_early_weight_loads_equal_waiting_loads(cuda, fp4, monkeypatch, m, n, k, bn):
+    # Right behind the activation quantizer, the CTA-pair kernel's B and
+    # scale-B producers load the cached weight before the programmatic wait;
+    # the bytes must equal a launch in which every role waits (FP4B_EARLY_B=0).
+    if bn:
+        monkeypatch.setenv("FP4B_FORCE_BN", bn)
+    x, w, b = W.cached_linear_inputs(m, n, k, seed=29)
+    with fp4.FP4WeightCache(w.to(cuda), b.to(cuda)) as cache:
+        xd = x.to(cuda)
+        monkeypatch.setenv("FP4B_EARLY_B", "0")
+        waiting = cache.forward(xd)
+        monkeypatch.delenv("FP4B_EARLY_B")
+        early = [cache.forward(xd) for _ in range(3)]
+        torch.cuda.synchronize()
+        for e in early:
+            assert torch.equal(e, waiting)
+        assert fp4.device_error() == 0
+
+
+def test_cached_linear_right_behind_an_unsynchronised_weight_quantize(cuda, fp4):
+    # fp4b_quantize_weights_ex(..., sync=0) returns with the weight quantizer
+    # still in flight; a cached linear enqueued right behind it on the same
+    # stream (activation quantizer, then the GEMM whose weight loads start
+    # before its programmatic wait) must read the finished cache.
+    m, n, k = 2048, 2880, 2880
+    lib = fp4._lib
+    st = torch.cuda.current_stream(cuda).cuda_stream
+    x = W.normal_bf16((m, k), 1.0, 31).to(cuda)
+    for seed in range(4):
+        w = W.normal_bf16((n, k), 0.02, 40 + seed).to(cuda)
+        with fp4.FP4WeightCache(w) as synced:
+            want = synced.forward(x)
+        torch.cuda.synchronize()
+        h = lib.fp4b_quantize_weights_ex(w.data_ptr(), n, k, k, st, 0)
+        assert h
+        try:
+            d = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+            assert lib.fp4b_run_cached_ex(x.data_ptr(), m, k, k, h, n, None, 0, d.data_ptr(), n, None, 1.0, 0.0,
+                                          st) == 0
+            torch.cuda.synchronize()
+        finally:
+            lib.fp4_weight_cache_free(h)
+        assert torch.equal(d, want)
+    assert fp4.device_error() == 0
+
+
 def test_global_scale_cache(cuda, fp4):
     # Opt-in two-level NVFP4 for N(0, 0.02) weights: the cache holds weight * s
     # (s a power of two) and every GEMM with it applies 1 / s.  Pearson with the
