@@ -207,9 +207,9 @@ __device__ __forceinline__ void store_chunk(const Params& p, const uint32_t (&r)
     }
 }
 
-// Copies bias[n0, n0 + bn) into `dst` as fp32 (zeros past N) with the lanes
-// of one warp, so the epilogue reads it from shared memory.
-__device__ __forceinline__ void stage_bias(const Params& p, float4* dst, int n0, int bn, int lane) {
+// Copies bias[n0, n0 + bn) into `dst` as BF16, 8 per uint4 (zeros past N),
+// with the lanes of one warp, so the epilogue reads it from shared memory.
+__device__ __forceinline__ void stage_bias(const Params& p, uint4* dst, int n0, int bn, int lane) {
     for (int i = lane; i < bn / 8; i += 32) {
         const int nb = n0 + 8 * i;
         uint4 v = make_uint4(0, 0, 0, 0);
@@ -219,12 +219,20 @@ __device__ __forceinline__ void stage_bias(const Params& p, float4* dst, int n0,
             __nv_bfloat16* vb = reinterpret_cast<__nv_bfloat16*>(&v);
             for (int j = 0; j < 8 && nb + j < p.n_out; ++j) vb[j] = p.bias[nb + j];
         }
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-        const float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
-        const float2 f2 = __bfloat1622float2(h[2]), f3 = __bfloat1622float2(h[3]);
-        dst[2 * i] = make_float4(f0.x, f0.y, f1.x, f1.y);
-        dst[2 * i + 1] = make_float4(f2.x, f2.y, f3.x, f3.y);
+        dst[i] = v;
     }
+}
+
+// Two BF16 additions, each rounded once from the exact sum.  For BF16 operands
+// this equals the reference's bias add (the BF16 values widened to fp32,
+// added, rounded to BF16): when their exponents differ by at most 16 the fp32
+// sum is exact, and otherwise the smaller operand is below 2^-16 of the larger,
+// whose BF16 neighbours are 2^-9 of it or more away, so both roundings return
+// the larger operand.
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
 }
 
 // Epilogue of one 32 x 32 chunk through shared memory: thread t converts row
@@ -238,7 +246,7 @@ __device__ __forceinline__ void stage_bias(const Params& p, float4* dst, int n0,
 // contents (chunk i - 1) waits until that store has read it.
 // Accumulator chunk (32 fp32 columns of this lane's row) -> 16 packed BF16
 // pairs: alpha, BF16, then the BF16 bias add of the reference.
-__device__ __forceinline__ void convert_chunk(const Params& p, const uint32_t (&r)[32], const float4* sbias,
+__device__ __forceinline__ void convert_chunk(const Params& p, const uint32_t (&r)[32], const uint4* sbias,
                                               uint32_t (&packed)[16]) {
     float v[32];
 #pragma unroll
@@ -250,17 +258,14 @@ __device__ __forceinline__ void convert_chunk(const Params& p, const uint32_t (&
 #pragma unroll
     for (int i = 0; i < 16; ++i) packed[i] = bf16x2_bits(v[2 * i], v[2 * i + 1]);
     if (p.bias) {
-        // Reference order: BF16 GEMM output, then a BF16 bias add (in fp32, rounded once).
+        // Reference order: BF16 GEMM output, then the BF16 bias add.
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-            const float4 b = sbias[g];
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const uint32_t x = packed[2 * g + h];
-                const float lo = __uint_as_float(x << 16) + (h ? b.z : b.x);
-                const float hi = __uint_as_float(x & 0xFFFF0000u) + (h ? b.w : b.y);
-                packed[2 * g + h] = bf16x2_bits(lo, hi);
-            }
+        for (int g = 0; g < 4; ++g) {
+            const uint4 b = sbias[g];
+            packed[4 * g + 0] = add_bf16x2(packed[4 * g + 0], b.x);
+            packed[4 * g + 1] = add_bf16x2(packed[4 * g + 1], b.y);
+            packed[4 * g + 2] = add_bf16x2(packed[4 * g + 2], b.z);
+            packed[4 * g + 3] = add_bf16x2(packed[4 * g + 3], b.w);
         }
     }
 }
@@ -623,7 +628,7 @@ struct PairCfg {
     static constexpr int BAR_BYTES = 256;
     // Epilogue staging: one 32 x 32 BF16 buffer (2 KB) and half the tile's bias per epilogue warp.
     static constexpr int EPI_BYTES = kPairEpiWarps * 2048;          // one 32 x 32 BF16 buffer per epilogue warp
-    static constexpr int BIAS_BYTES = kPairEpiWarps * (TW / 2) * 4;  // fp32 bias of each warp's half of the tile
+    static constexpr int BIAS_BYTES = kPairEpiWarps * (TW / 2) * 2;  // BF16 bias of each warp's half of the tile
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + BIAS_BYTES + BAR_BYTES + 1024;
     static constexpr int SF_COLS = 4 * kKbPerStage * (1 + NRT);
     static constexpr int ACC_BUFS = (2 * TW + SF_COLS <= (int)kTmemCols) ? 2 : 1;
@@ -725,12 +730,12 @@ __device__ __forceinline__ void quantize_phase(const Params& p, const qcore::Sme
 // quadrant q: the two epilogue warps q and q + 4 (members 0, 1) and the warps
 // whose roles have ended (8 and 12 on quadrant 0, 9, 10, 11 on quadrants 1-3).
 // Member ti of ts takes 32-column chunks c = ti, ti + ts, ...
-// Chunk c's fp32 bias was staged by epilogue warp q + 4 (c & 1) at float4
-// offset 8 (c >> 1).  tq: TMEM address of the quadrant's accumulator; buf: the
+// Chunk c's BF16 bias was staged by epilogue warp q + 4 (c & 1) at uint4
+// offset 4 (c >> 1).  tq: TMEM address of the quadrant's accumulator; buf: the
 // member's 2 KB staging buffer; m: this lane's output row.
 template <int TW>
 __device__ __forceinline__ void team_epilogue(const Params& p, const CUtensorMap* tmap_d, uint32_t tq,
-                                              const float4* sBias, int q, int ti, int ts, uint8_t* buf,
+                                              const uint4* sBias, int q, int ti, int ts, uint8_t* buf,
                                               int& chunk_iter, int m, int n0, int lane) {
     constexpr int CH = TW / 32;
 #pragma unroll 1
@@ -741,7 +746,7 @@ __device__ __forceinline__ void team_epilogue(const Params& p, const CUtensorMap
         if (n0 + 32 * c >= p.n_out) continue;
         if (p.tma_store) {
             uint32_t pk[16];
-            convert_chunk(p, r, sBias + (q + 4 * (c & 1)) * (TW / 8) + 8 * (c >> 1), pk);
+            convert_chunk(p, r, sBias + (q + 4 * (c & 1)) * (TW / 16) + 4 * (c >> 1), pk);
             if (m - lane < p.m)  // the warp's 32 rows start inside D
                 store_staged_chunk(p, tmap_d, pk, buf, m - lane, n0 + 32 * c, lane, chunk_iter++);
         } else if (m < p.m) {
@@ -766,7 +771,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     uint8_t* sSFA = sB + STAGES * C::B_BYTES;
     uint8_t* sSFB = sSFA + STAGES * C::SFA_BYTES;
     uint8_t* sEpi = sSFB + STAGES * C::SFB_BYTES;
-    float4* sBias = reinterpret_cast<float4*>(sEpi + C::EPI_BYTES);
+    uint4* sBias = reinterpret_cast<uint4*>(sEpi + C::EPI_BYTES);
     uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + C::EPI_BYTES + C::BIAS_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;     // [2]
@@ -991,7 +996,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         constexpr int kMyChunks = TW / 64;
         const uint32_t acc_empty0 = ptx::map_to_cta(ptx::smem_u32(acc_empty), 0);
         uint8_t* epi = sEpi + warp * 2048;
-        float4* wbias = sBias + warp * (TW / 8);
+        uint4* wbias = sBias + warp * (TW / 16);
         if constexpr (FUSED) {
             // The quantizer tables live in the (not yet used) epilogue staging buffers.
             static_assert(C::EPI_BYTES >= qcore::kSmemTableBytes, "tables must fit the staging buffers");
@@ -1012,7 +1017,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             if (p.bias) {
                 __syncwarp();  // the previous tile's reads of wbias are done
 #pragma unroll
-                for (int j = 0; j < kMyChunks; ++j) stage_bias(p, wbias + 8 * j, n0 + 32 * (h + 2 * j), 32, lane);
+                for (int j = 0; j < kMyChunks; ++j) stage_bias(p, wbias + 4 * j, n0 + 32 * (h + 2 * j), 32, lane);
                 __syncwarp();
             }
             if (last_tile && lane == 0) ptx::mbar_arrive(bias_ready);
@@ -1055,8 +1060,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 ptx::tmem_ld_wait();
                 if (p.tma_store) {
                     uint32_t pa[16], pb[16];
-                    convert_chunk(p, ra, wbias + 8 * j, pa);
-                    if (two) convert_chunk(p, rb, wbias + 8 * (j + 1), pb);
+                    convert_chunk(p, ra, wbias + 4 * j, pa);
+                    if (two) convert_chunk(p, rb, wbias + 4 * (j + 1), pb);
                     if (j + 2 < kMyChunks) {
                         ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 2), ra);
                         if (j + 3 < kMyChunks) ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 3), rb);

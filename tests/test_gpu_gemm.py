@@ -171,3 +171,29 @@ def test_wide_pair_tile_equals_default(cuda, fp4, monkeypatch, m, n, k):
     if m * n * k < 1e9:
         assert_gemm_close(wide, oracle_linear(x, w, bias=b), f"384-wide {m}x{n}x{k}")
     assert fp4.device_error() == 0
+
+
+@pytest.mark.parametrize("pair,bn", [(0, 128), (1, 128), (1, 192), (1, 256), (1, 384)])
+@pytest.mark.parametrize("m,n,k,alpha", [(2048, 2880, 7680, 1.0), (300, 1000, 640, 0.37), (4096, 640, 1024, 1.0)])
+def test_bias_add_equals_bf16_add_of_unbiased_output(cuda, fp4, monkeypatch, pair, bn, m, n, k, alpha):
+    # The reference adds the bias to the BF16 GEMM output in BF16 (fp32 sum,
+    # one rounding).  Every epilogue must give exactly torch's BF16 add of its
+    # own unbiased output and the bias, for biases over 80 binades (sums that
+    # are exact in fp32, and ones where the smaller operand vanishes), zeros
+    # and +-inf.
+    if pair == 0 and m > 128 and bn == 128:
+        m = 128  # the one-CTA kernel's own shape range
+    monkeypatch.setenv("FP4B_PAIR", str(pair))
+    monkeypatch.setenv("FP4B_FORCE_BN", str(bn))
+    x = W.normal_bf16((m, k), 1.0, 81)
+    w = W.normal_bf16((n, k), 1.0, 82)
+    g = torch.Generator().manual_seed(83)
+    b = torch.randn(n, generator=g) * torch.exp2(torch.randint(-40, 41, (n,), generator=g).float())
+    b[::97] = 0.0
+    b[5], b[6] = float("inf"), float("-inf")
+    b = b.to(torch.bfloat16)
+    plain = run_prequant(fp4, x, w, alpha=alpha)
+    biased = run_prequant(fp4, x, w, bias=b, alpha=alpha)
+    want = (plain.float() + b.to(plain.device).float()).to(torch.bfloat16)
+    assert torch.equal(biased, want)
+    assert fp4.device_error() == 0
