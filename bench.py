@@ -458,7 +458,7 @@ def run_ours(args):
             "kernels": {"quantize_activations_us": quant_ms * 1e3, "gemm_us": gemm_ms * 1e3,
                         "step_us": ms_per_step * 1e3,
                         "quantize_activations_gbs": quant_bytes / (quant_ms * 1e-3) / 1e9},
-            "roofline": {"bound": "tensor", "kernel": "nvf4_gemm_pair_kernel (2048x2880x7680, 256x384 CTA-pair tiles)",
+            "roofline": {"bound": "tensor", "kernel": "nvf4_gemm_pair_kernel (2048x2880x7680, 256x320 CTA-pair tiles, N = 128 + 192 MMAs per k-block)",
                          "achieved": gemm_tflops, "peak": fp4_peak, "unit": "TFLOP/s",
                          "frac": gemm_tflops / fp4_peak, "traffic": traffic,
                          "peak_source": f"4 x bf16 dense burst ({peaks['source']}, MEASURED_PEAKS.json): "

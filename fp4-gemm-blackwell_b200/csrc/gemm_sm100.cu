@@ -604,21 +604,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 // that has not issued for 32 stages.
 constexpr int kPairEpiWarps = 8;  // two per TMEM lane quadrant, each storing half of the columns
 
-// A pair tile is 256 x TW with TW = NSUB * BN: NSUB MMAs of N = BN per k-block
-// share the A tile (NSUB = 2 moves a third fewer operand bytes per column; its
-// accumulator is single-buffered, so it suits problems whose tiles fit in one
-// round of CTA pairs).
-template <int BN, int STAGES, int NSUB = 1>
+// A pair tile is 256 x TW: with NSUB = 2, two MMAs per k-block (N = BN on
+// columns [0, BN), N = BN1 on [BN, BN + BN1)) share the A tile, which moves
+// fewer operand bytes per column; its accumulator is single-buffered, so it
+// suits problems whose tiles fit in one round of CTA pairs.
+template <int BN, int STAGES, int NSUB = 1, int BN1 = BN>
 struct PairCfg {
     static constexpr int kKbPerStage = 4;   // a stage covers K = 256: one 128-byte chunk
     static_assert(BN % 64 == 0 && BN >= 128 && BN <= 256, "BN must be 128, 192 or 256");
+    static_assert(BN1 % 64 == 0 && BN1 >= 128 && BN1 <= 256, "BN1 must be 128, 192 or 256");
     static_assert(NSUB == 1 || NSUB == 2, "one or two MMAs per k-block");
-    static constexpr int TW = NSUB * BN;    // tile width
-    static constexpr int BH = BN / 2;       // B rows of one MMA held by each CTA
+    static_assert(NSUB == 2 || BN1 == BN, "a second width needs a second MMA");
+    static constexpr int TW = BN + (NSUB - 1) * BN1;  // tile width
+    static constexpr int BH = BN / 2;       // B rows of the first MMA held by each CTA
+    static constexpr int BH1 = BN1 / 2;     // B rows of the second MMA held by each CTA
     static constexpr int NRT = max_row_tiles(TW);
     static constexpr int A_BYTES = kBM * kChunkBytes;
     static constexpr int B_SUB_BYTES = BH * kChunkBytes;
-    static constexpr int B_BYTES = NSUB * B_SUB_BYTES;
+    static constexpr int B_SUB1_BYTES = BH1 * kChunkBytes;
+    static constexpr int B_BYTES = B_SUB_BYTES + (NSUB - 1) * B_SUB1_BYTES;
     static constexpr int SFA_BYTES = kKbPerStage * kAtomBytes;
     static constexpr int SFB_BYTES = NRT * kKbPerStage * kAtomBytes;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
@@ -634,7 +638,7 @@ struct PairCfg {
     static constexpr int ACC_BUFS = (2 * TW + SF_COLS <= (int)kTmemCols) ? 2 : 1;
     static constexpr uint32_t TMEM_SFA = ACC_BUFS * TW;
     static constexpr uint32_t TMEM_SFB = TMEM_SFA + 4 * kKbPerStage;
-    static_assert(B_SUB_BYTES % 1024 == 0, "B stage must keep the 128B-swizzle alignment");
+    static_assert(B_SUB_BYTES % 1024 == 0 && B_SUB1_BYTES % 1024 == 0, "B stage must keep the 128B-swizzle alignment");
     static_assert(STAGE_BYTES % 1024 == 0, "epilogue buffers must stay 1024-byte aligned");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
     static_assert(TMEM_SFA + SF_COLS <= kTmemCols, "TMEM budget exceeded");
@@ -755,12 +759,13 @@ __device__ __forceinline__ void team_epilogue(const Params& p, const CUtensorMap
     }
 }
 
-template <int BN, int STAGES, bool FUSED, int NSUB>
+template <int BN, int STAGES, bool FUSED, int NSUB, int BN1>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     nvf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                          const __grid_constant__ CUtensorMap tmap_b1,
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
                           const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ Params p) {
-    using C = PairCfg<BN, STAGES, NSUB>;
+    using C = PairCfg<BN, STAGES, NSUB, BN1>;
     constexpr int TW = C::TW;
     constexpr int TILE_M = 2 * kBM;
     constexpr int kKbPerStage = C::kKbPerStage;
@@ -804,6 +809,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         ptx::fence_mbar_init();
         ptx::prefetch_tmap(&tmap_a);
         ptx::prefetch_tmap(&tmap_b);
+        if (NSUB > 1) ptx::prefetch_tmap(&tmap_b1);
         ptx::prefetch_tmap(&tmap_sfa);
         ptx::prefetch_tmap(&tmap_sfb);
         if (p.tma_store) ptx::prefetch_tmap(&tmap_d);
@@ -891,8 +897,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                         if (rank == 0) ptx::mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
                         ptx::tma_load_2d_pair(sA + s * C::A_BYTES, &tmap_a, bar, kx, a_row);
                     } else if (role == 1) {
-                        ptx::tma_load_2d_pair(sB + s * C::B_BYTES + sub * C::B_SUB_BYTES, &tmap_b, bar, kx,
-                                              b_row + sub * BN);
+                        if (sub == 0)
+                            ptx::tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_b, bar, kx, b_row);
+                        else  // the second MMA's rows [n0 + BN, n0 + TW), split between the CTAs
+                            ptx::tma_load_2d_pair(sB + s * C::B_BYTES + C::B_SUB_BYTES, &tmap_b1, bar, kx,
+                                                  n0 + BN + (int)rank * C::BH1);
                     } else if (role == 2) {
                         ptx::tma_load_3d_pair(sSFA + s * C::SFA_BYTES, &tmap_sfa, bar, 0, kb0, sfa_rt);
                     } else {
@@ -910,6 +919,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             const uint64_t sfadesc0 = ptx::desc_sf_atom(ptx::smem_u32(sSFA));
             const uint64_t sfbdesc0 = ptx::desc_sf_atom(ptx::smem_u32(sSFB));
             constexpr uint32_t idesc = ptx::idesc_nvf4(BN, 2 * kBM);
+            constexpr uint32_t idesc1 = ptx::idesc_nvf4(BN1, 2 * kBM);
             int it = 0, tile_iter = 0;
             bool stop = false;
             for (int t = pair; t < p.num_tiles && !stop; t += npairs, ++tile_iter) {
@@ -971,8 +981,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
 #pragma unroll
                                 for (int u = 0; u < NSUB; ++u)
                                     ptx::tc_mma_nvf4_pair(acc + u * BN, a_s + koff,
-                                                          b_s + (uint64_t)((u * C::B_SUB_BYTES) >> 4) + koff, idesc,
-                                                          sfa_t + 4 * j,
+                                                          b_s + (uint64_t)((u * C::B_SUB_BYTES) >> 4) + koff,
+                                                          u == 0 ? idesc : idesc1, sfa_t + 4 * j,
                                                           sfb_t + j * 4 * C::NRT + shift_words + (u * BN) / 32,
                                                           (j == 0) ? first : 1u);
                             }
@@ -1286,20 +1296,21 @@ int max_pairs(K kernel, int smem, int sms) {
     return c;
 }
 
-template <int BN, int STAGES, bool FUSED = false, int NSUB = 1>
+template <int BN, int STAGES, bool FUSED = false, int NSUB = 1, int BN1 = BN>
 cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const QuantizeArgs* qa = nullptr,
                         uint32_t* sync_words = nullptr, void* const* peers = nullptr, int npeers = 0) {
-    using C = PairCfg<BN, STAGES, NSUB>;
-    auto kernel = nvf4_gemm_pair_kernel<BN, STAGES, FUSED, NSUB>;
+    using C = PairCfg<BN, STAGES, NSUB, BN1>;
+    auto kernel = nvf4_gemm_pair_kernel<BN, STAGES, FUSED, NSUB, BN1>;
     static std::once_flag attr_once[64];
     int dev = 0;
     cudaGetDevice(&dev);
     std::call_once(attr_once[dev & 63], [&] {
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     });
-    CUtensorMap ma, mb, msa, msb, md;
+    CUtensorMap ma, mb, mb1, msa, msb, md;
     if (!make_operand_map(&ma, g.a_fp4, g.m_rows_pad, g.k_pad, kBM) ||
         !make_operand_map(&mb, g.b_fp4, g.n_rows_pad, g.k_pad, C::BH) ||
+        !make_operand_map(&mb1, g.b_fp4, g.n_rows_pad, g.k_pad, C::BH1) ||
         !make_scale_map(&msa, g.a_sf, g.m_rows_pad, g.k_pad, C::kKbPerStage, 1) ||
         !make_scale_map(&msb, g.b_sf, g.n_rows_pad, g.k_pad, C::kKbPerStage, C::NRT))
         return cudaErrorInvalidValue;
@@ -1322,7 +1333,8 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const Q
     }
     const int pairs = max_pairs(kernel, C::SMEM_BYTES, sms);
     const int grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);
-    return launch_dependent(kernel, dim3(grid), dim3(kPairThreads), C::SMEM_BYTES, stream, ma, mb, msa, msb, md, p);
+    return launch_dependent(kernel, dim3(grid), dim3(kPairThreads), C::SMEM_BYTES, stream, ma, mb, mb1, msa, msb, md,
+                            p);
 }
 
 template <int BN, int STAGES, int CHUNKS>
@@ -1371,12 +1383,16 @@ int choose_bn(long m, long n, int sms) {
 // 256 x 384 tile (two N = 192 MMAs per k-block on one A tile: a third fewer
 // operand bytes per column); per-round overhead ~1 us with two accumulators in
 // TMEM (the epilogue overlaps the next tile), 2.1 us for BN = 256 and 4.2 us
-// for the 384-wide tile, whose single accumulator exposes every epilogue.
-// Returns 128, 192, 256 or 384 (= 2 x 192).
+// for the 384-wide tile, whose single accumulator exposes every epilogue.  The
+// 256 x 320 tile (N = 128 + 192) takes nearly the 384-wide tile's time per
+// stage (0.526 against 0.533 us on 2048 x 2880 x {2880, 7680}: the mainloop
+// is bound by operand delivery, which is mostly A) and less per round; it
+// wins where it needs no more rounds, e.g. 72 tiles for N = 2880 on 74 pairs.
+// Returns 128, 192, 256, 320 (= 128 + 192) or 384 (= 2 x 192).
 int choose_bn_pair(long m, long n, long k_pad, int sms) {
     struct Width { int code; double stage_us, round_us, fixed_us; };
-    static const Width cands[] = {{384, 0.55, 4.2, 3.0}, {256, 0.44, 2.06, 5.0}, {192, 0.37, 1.0, 5.0},
-                                  {128, 0.30, 1.0, 5.0}};
+    static const Width cands[] = {{384, 0.55, 4.2, 3.0}, {320, 0.54, 3.9, 3.0}, {256, 0.44, 2.06, 5.0},
+                                  {192, 0.37, 1.0, 5.0}, {128, 0.30, 1.0, 5.0}};
     const long mt = (m + 2 * kBM - 1) / (2 * kBM);
     const long pairs = sms / 2 > 0 ? sms / 2 : 1;
     const double stages = (double)((k_pad + 255) / 256);
@@ -1415,7 +1431,8 @@ cudaError_t gemm_launch_fused(const GemmArgs& g, const QuantizeArgs& qa, uint32_
         case 256: return launch_pair<256, 5, true>(g, stream, sms, &qa, sync_words);
         case 192: return launch_pair<192, 6, true>(g, stream, sms, &qa, sync_words);
         case 128: return launch_pair<128, 7, true>(g, stream, sms, &qa, sync_words);
-        case 384: return launch_pair<192, 6, true>(g, stream, sms, &qa, sync_words);  // no fused 384-wide tile
+        case 384:  // no fused two-MMA tiles
+        case 320: return launch_pair<192, 6, true>(g, stream, sms, &qa, sync_words);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -1432,6 +1449,7 @@ cudaError_t gemm_launch_peers(const GemmArgs& g, void* const* peers, int npeers,
         case 192: return launch_pair<192, 6, false>(g, stream, sms, nullptr, nullptr, peers, npeers);
         case 128: return launch_pair<128, 7, false>(g, stream, sms, nullptr, nullptr, peers, npeers);
         case 384: return launch_pair<192, 4, false, 2>(g, stream, sms, nullptr, nullptr, peers, npeers);
+        case 320: return launch_pair<128, 4, false, 2, 192>(g, stream, sms, nullptr, nullptr, peers, npeers);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -1466,6 +1484,7 @@ cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream) {
             case 192: return launch_pair<192, 6, false>(g, stream, sms);
             case 128: return launch_pair<128, 7, false>(g, stream, sms);
             case 384: return launch_pair<192, 4, false, 2>(g, stream, sms);
+            case 320: return launch_pair<128, 4, false, 2, 192>(g, stream, sms);
             default: return cudaErrorInvalidValue;
         }
     }

@@ -154,26 +154,29 @@ def test_dequant_torch_matches_oracle(cuda, fp4):
 
 @pytest.mark.parametrize("m,n,k", [(256, 384, 512), (300, 1000, 640), (257, 769, 256), (2304, 3200, 512),
                                    (2048, 2880, 7680)])
-def test_wide_pair_tile_equals_default(cuda, fp4, monkeypatch, m, n, k):
-    # The 256 x 384 pair tile (two N = 192 MMAs per k-block on one A tile, one
-    # TMEM accumulator) runs the same K sequence per output element as the
-    # other widths, so its bytes equal theirs; also close to the oracle, and
-    # several tiles per pair (2304 x 3200) reuse the single accumulator.
+@pytest.mark.parametrize("width", ["384", "320"])
+def test_wide_pair_tile_equals_default(cuda, fp4, monkeypatch, m, n, k, width):
+    # The 256 x 384 and 256 x 320 pair tiles (two MMAs per k-block on one A
+    # tile, N = 192 + 192 or 128 + 192, one TMEM accumulator) run the same K
+    # sequence per output element as the other widths, so their bytes equal
+    # theirs; also close to the oracle, and several tiles per pair
+    # (2304 x 3200) reuse the single accumulator.  320-wide tiles start 0 or
+    # 64 rows into a 128-row scale atom.
     x = W.normal_bf16((m, k), 1.0, 71)
     w = W.normal_bf16((n, k), 1.0, 72)
     b = W.normal_bf16((n,), 1.0, 73)
     monkeypatch.setenv("FP4B_PAIR", "1")
     monkeypatch.setenv("FP4B_FORCE_BN", "192")
     narrow = run_prequant(fp4, x, w, bias=b)
-    monkeypatch.setenv("FP4B_FORCE_BN", "384")
+    monkeypatch.setenv("FP4B_FORCE_BN", width)
     wide = run_prequant(fp4, x, w, bias=b)
     assert torch.equal(wide, narrow)
     if m * n * k < 1e9:
-        assert_gemm_close(wide, oracle_linear(x, w, bias=b), f"384-wide {m}x{n}x{k}")
+        assert_gemm_close(wide, oracle_linear(x, w, bias=b), f"{width}-wide {m}x{n}x{k}")
     assert fp4.device_error() == 0
 
 
-@pytest.mark.parametrize("pair,bn", [(0, 128), (1, 128), (1, 192), (1, 256), (1, 384)])
+@pytest.mark.parametrize("pair,bn", [(0, 128), (1, 128), (1, 192), (1, 256), (1, 320), (1, 384)])
 @pytest.mark.parametrize("m,n,k,alpha", [(2048, 2880, 7680, 1.0), (300, 1000, 640, 0.37), (4096, 640, 1024, 1.0)])
 def test_bias_add_equals_bf16_add_of_unbiased_output(cuda, fp4, monkeypatch, pair, bn, m, n, k, alpha):
     # The reference adds the bias to the BF16 GEMM output in BF16 (fp32 sum,
