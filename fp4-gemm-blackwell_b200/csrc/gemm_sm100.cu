@@ -1376,22 +1376,23 @@ int choose_bn(long m, long n, int sms) {
 
 // Tile width of the CTA-pair kernel: the one with the smallest modelled time,
 //   rounds x (stages x stage time + per-round overhead) + fixed cost,
-// rounds = ceil(tiles / pairs), a stage = K of 256.  Fitted to back-to-back
-// B200 runs of this kernel on seven shapes from 512x2880x2880 to 8192^3 (each
-// within ~8 % of the fit): stage time 0.30 / 0.37 / 0.44 us for BN = 128 /
-// 192 / 256 (the TMA ring and the tensor pipe, both ~busy) and 0.55 us for the
-// 256 x 384 tile (two N = 192 MMAs per k-block on one A tile: a third fewer
-// operand bytes per column); per-round overhead ~1 us with two accumulators in
-// TMEM (the epilogue overlaps the next tile), 2.1 us for BN = 256 and 4.2 us
-// for the 384-wide tile, whose single accumulator exposes every epilogue.  The
-// 256 x 320 tile (N = 128 + 192) takes nearly the 384-wide tile's time per
-// stage (0.526 against 0.533 us on 2048 x 2880 x {2880, 7680}: the mainloop
-// is bound by operand delivery, which is mostly A) and less per round; it
-// wins where it needs no more rounds, e.g. 72 tiles for N = 2880 on 74 pairs.
+// rounds = ceil(tiles / pairs), a stage = K of 256, fitted to back-to-back
+// B200 runs from 512x2880x2880 to 8192^3 (each within ~5 % of the fit).
+// BN = 128 / 192 / 256: stage time 0.30 / 0.37 / 0.44 us (the TMA ring and the
+// tensor pipe, both ~busy), per-round overhead ~1 us with two accumulators in
+// TMEM (the epilogue overlaps the next tile) and 2.1 us for BN = 256.  The
+// two-MMA tiles (one A tile shared by an N = 192 + 192 or 128 + 192 pair of
+// MMAs, a single accumulator) take nearly the same time per stage whatever
+// their width, as operand delivery sets the pace: 0.58 / 0.53 us for 384 /
+// 320 with 2.3 / 3.2 us per round (part of each exposed epilogue overlaps the
+// next tile's first loads), fitted on 8192x15360x2880, 8192^3, the headline
+// and 4096x2880x7680.  The 320-wide tile wins where it needs no more rounds,
+// e.g. 72 tiles for N = 2880 on 74 pairs; the 384-wide one on short-K
+// many-round shapes (8192x15360x2880: 170 us against 191 us with BN = 192).
 // Returns 128, 192, 256, 320 (= 128 + 192) or 384 (= 2 x 192).
 int choose_bn_pair(long m, long n, long k_pad, int sms) {
     struct Width { int code; double stage_us, round_us, fixed_us; };
-    static const Width cands[] = {{384, 0.55, 4.2, 3.0}, {320, 0.54, 3.9, 3.0}, {256, 0.44, 2.06, 5.0},
+    static const Width cands[] = {{384, 0.58, 2.3, 3.0}, {320, 0.53, 3.2, 3.0}, {256, 0.44, 2.06, 5.0},
                                   {192, 0.37, 1.0, 5.0}, {128, 0.30, 1.0, 5.0}};
     const long mt = (m + 2 * kBM - 1) / (2 * kBM);
     const long pairs = sms / 2 > 0 ? sms / 2 : 1;
