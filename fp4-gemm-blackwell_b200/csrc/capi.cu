@@ -492,6 +492,14 @@ FP4B_EXPORT int fp4_gemm_run_cached(const void* A, const void* h, const void* C,
 
 FP4B_EXPORT int fp4b_version(void) { return 1; }
 
+FP4B_EXPORT int fp4b_gemm_tile_width(int m, int n, int k, int sms) {
+    if (m <= 0 || n <= 0 || k <= 0 || sms < 2) {
+        set_last_error("fp4b_gemm_tile_width: m, n, k must be positive and sms at least 2");
+        return -1;
+    }
+    return gemm_tile_width(m, n, round_up(k, 128), sms);
+}
+
 FP4B_EXPORT const char* fp4b_last_error(void) { return t_last_error; }
 
 FP4B_EXPORT int fp4b_device_error(int clear) {

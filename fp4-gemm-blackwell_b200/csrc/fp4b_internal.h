@@ -47,6 +47,10 @@ struct GemmArgs {
 };
 
 const char* gemm_check(const GemmArgs& g);
+// Output columns per tile that gemm_launch picks without FP4B_PAIR / FP4B_FORCE_BN:
+// the CTA-pair kernel's 128 / 192 / 256 / 320 / 384 for m > 128, else the
+// one-CTA kernel's 128 / 192 / 256; -1 on bad arguments.  Host only.
+int gemm_tile_width(long m, long n, long k_pad, int sms);
 cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream);
 
 // Cached linear with the activation quantization inside the GEMM kernel (the

@@ -1455,6 +1455,11 @@ cudaError_t gemm_launch_peers(const GemmArgs& g, void* const* peers, int npeers,
     }
 }
 
+int gemm_tile_width(long m, long n, long k_pad, int sms) {
+    if (m <= 0 || n <= 0 || k_pad <= 0 || k_pad % 128 || sms < 2) return -1;
+    return m > kBM ? choose_bn_pair(m, n, k_pad, sms) : choose_bn(m, n, sms);
+}
+
 const char* gemm_check(const GemmArgs& g) {
     if (!g.a_fp4 || !g.a_sf || !g.b_fp4 || !g.b_sf || !g.d) return "null pointer";
     if (g.m <= 0 || g.n_out <= 0) return "empty problem";

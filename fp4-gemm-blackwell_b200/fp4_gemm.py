@@ -63,6 +63,7 @@ _bind("fp4_weight_cache_sf_ptr", _vp, [_vp])
 _bind("fp4_gemm_run_cached", _i, [_vp, _vp, _vp, _vp, _i, _f, _f])
 # Additive ABI.
 _bind("fp4b_version", _i, [])
+_bind("fp4b_gemm_tile_width", _i, [_i, _i, _i, _i])
 _bind("fp4b_last_error", ctypes.c_char_p, [])
 _bind("fp4b_device_error", _i, [_i])
 _bind("fp4b_quantize", _i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp])
@@ -650,6 +651,16 @@ def gemm_prequantized(a_fp4, a_sf, m: int, b_fp4, b_sf, n: int, k_pad: int, bias
     if rc != 0:
         raise RuntimeError(f"fp4b_gemm_prequant failed with error code {rc} ({_last_error()})")
     return D
+
+
+def gemm_tile_width(m: int, n: int, k: int, sms: int = 148) -> int:
+    """Output columns per tile the GEMM's time model picks for M x N x K on a
+    device with `sms` SMs (no device work): 128 / 192 / 256, or the two-MMA
+    320 / 384 on CTA pairs when M > 128."""
+    w = _lib.fp4b_gemm_tile_width(m, n, k, sms)
+    if w < 0:
+        raise ValueError(f"gemm_tile_width: {_last_error()}")
+    return w
 
 
 def device_error(clear: bool = True) -> int:

@@ -94,6 +94,14 @@ int fp4_gemm_run_cached(const void* A_bf16, const void* cache_handle, const void
 /* Library ABI version (1). */
 int fp4b_version(void);
 
+/* Output columns per tile the GEMM picks for an M x N x K problem (K padded to
+ * 128) on a device with `sms` SMs, from its time model and without the
+ * FP4B_PAIR / FP4B_FORCE_BN overrides: 128 / 192 / 256 (one MMA per k-block),
+ * 320 (128 + 192) or 384 (192 + 192) on CTA pairs when M > 128, else the
+ * one-CTA kernel's 128 / 192 / 256.  -1 on bad arguments.  Host only: no
+ * device work, no GPU needed. */
+int fp4b_gemm_tile_width(int m, int n, int k, int sms);
+
 /* Message of the last failed call on this host thread ("" if none). */
 const char* fp4b_last_error(void);
 

@@ -44,3 +44,23 @@ def test_global_scale_reduces_error_of_small_weights_in_the_oracle():
     e0 = rms(O.dequantize(q0, f0, 256, 1024))
     e1 = rms(O.dequantize(q1, f1, 256, 1024) / s)
     assert e1 < 0.85 * e0, (e0, e1)  # measured 0.129 -> 0.095
+
+
+def test_gemm_tile_width_model_decisions():
+    # The tile width the GEMM picks from its time model (host only), for the
+    # shapes it was fitted on, with B200's 148 SMs: the 320-wide two-MMA tile
+    # for the headline (72 tiles on 74 CTA pairs), the 384-wide one for
+    # short-K many-round shapes (config-5 gate_up, 8192^3), narrower tiles for
+    # small M, the one-CTA kernel's widths for M <= 128.
+    import pytest
+
+    import fp4_gemm
+    want = {(2048, 2880, 7680): 320, (4096, 2880, 7680): 320, (8192, 15360, 2880): 384, (8192, 5120, 2880): 384,
+            (8192, 8192, 8192): 384, (16384, 16384, 16384): 384, (2048, 5120, 2880): 192, (1024, 2880, 7680): 192,
+            (512, 2880, 2880): 128, (256, 2880, 2880): 128}
+    got = {s: fp4_gemm.gemm_tile_width(*s) for s in want}
+    assert got == want
+    assert fp4_gemm.gemm_tile_width(128, 2880, 2880) in (128, 192, 256)
+    assert fp4_gemm.gemm_tile_width(1, 8, 128) in (128, 192, 256)
+    with pytest.raises(ValueError):
+        fp4_gemm.gemm_tile_width(0, 128, 128)
