@@ -1,6 +1,6 @@
 """Multi-GPU NVFP4 linear layers on one node (one process per GPU).
 
-The reference runs on one device (SURVEY: no collective anywhere).  Two ways
+The reference runs on one device (it has no collective anywhere).  Two ways
 to spread the cached linear over the GPUs of a node, both built on the
 single-GPU kernels of ``fp4_gemm``:
 

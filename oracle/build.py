@@ -28,7 +28,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "libnvfp4_oracle.so")
 REF_DIR = os.path.join(HERE, "_ref")
 REF_SO = os.path.join(REF_DIR, "libref_quant.so")
-REFERENCE_LIB_CU = os.environ.get("FP4_REFERENCE_LIB_CU", "/root/reference/fp4_gemm_lib.cu")
+# The reference checkout sits beside this repository ("reference/"); FP4_REFERENCE_LIB_CU overrides it.
+REFERENCE_LIB_CU = os.environ.get(
+    "FP4_REFERENCE_LIB_CU",
+    os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference", "fp4_gemm_lib.cu"))
 
 # Both compiles keep IEEE fp32 semantics: no contraction, no fast-math.
 _FP_FLAGS = ["-O2", "-ffp-contract=off", "-fno-fast-math", "-fopenmp", "-fPIC", "-shared"]
