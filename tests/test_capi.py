@@ -84,3 +84,37 @@ def test_python_argument_errors_match_reference():
         fp4_gemm.fp4_matmul(torch.zeros(4, 8), torch.zeros(4, 16))
     with pytest.raises(AssertionError, match="Both tensors must be on CUDA"):
         fp4_gemm.fp4_matmul(torch.zeros(4, 8), torch.zeros(4, 8))
+
+
+_ALLOC_FAILURE_SCRIPT = r"""
+import ctypes, sys
+lib = ctypes.CDLL(sys.argv[1])
+lib.fp4_quantize_weights.restype = ctypes.c_void_p
+lib.fp4b_last_error.restype = ctypes.c_char_p
+buf = ctypes.create_string_buffer(128 * 128 * 2)
+p = ctypes.cast(buf, ctypes.c_void_p)
+one, zero = ctypes.c_float(1.0), ctypes.c_float(0.0)
+res = [lib.fp4_quantize_weights(p, 128, 128) is None, lib.fp4b_last_error()]
+res += [lib.fp4_gemm_init(128, 128, 128), lib.fp4b_last_error()]
+res += [lib.fp4_gemm_prealloc(128, 128, 128), lib.fp4_gemm_run(p, p, None, p, 128, 128, 128, one, zero)]
+lib.fp4_gemm_cleanup()
+print(repr(res))
+"""
+
+
+def test_allocation_failures_return_errors():
+    # Host-side fault injection: with no device visible every cudaMalloc the
+    # library makes fails.  The calls that allocate must return their error
+    # value with a message (where the reference leaves cudaMalloc unchecked,
+    # fp4_gemm_lib.cu:467-470) and leave the process usable.
+    import ast
+    import subprocess
+    import sys
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    out = subprocess.run([sys.executable, "-c", _ALLOC_FAILURE_SCRIPT, LIB], env=env, capture_output=True, text=True,
+                         timeout=120)
+    assert out.returncode == 0, out.stderr[-2000:]
+    null_cache, msg_q, rc_init, msg_init, rc_pre, rc_run = ast.literal_eval(out.stdout.strip().splitlines()[-1])
+    assert null_cache and b"cudaMalloc" in msg_q
+    assert rc_init == -1 and b"cudaMalloc" in msg_init
+    assert rc_pre == -1 and rc_run == -1
