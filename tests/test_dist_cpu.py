@@ -87,3 +87,41 @@ def test_gather_columns_two_ranks_gloo(n):
     results = [q.get(timeout=10) for _ in procs]
     assert all(ok for _, ok, _ in results), results
     assert all(shape == (37, n) for _, _, shape in results)
+
+
+def _leaving_worker(rank, world, port, q):
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        os._exit(0)  # this rank leaves between steps, before its next collective
+    shards = D.plan_column_shards(300, world)
+    local = torch.zeros(5, shards[rank].cols)
+    try:
+        D.gather_columns(local, shards)
+        q.put((rank, "returned"))
+    except Exception as e:  # the survivor's collective ends with an error instead of waiting for good
+        q.put((rank, type(e).__name__))
+    os._exit(0)
+
+
+def test_rank_that_leaves_ends_the_survivors_collective_with_an_error():
+    # Failure detection on the host: when one rank leaves, the other rank's
+    # next collective (the column all-gather) raises within the process
+    # group's short timeout rather than hanging.
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.exitcode is None:
+            p.kill()
+    assert codes == [0, 0], f"rank exit codes {codes}"
+    rank, outcome = q.get(timeout=10)
+    assert rank == 0 and outcome != "returned", outcome
