@@ -64,6 +64,7 @@ _bind("fp4_gemm_run_cached", _i, [_vp, _vp, _vp, _vp, _i, _f, _f])
 # Additive ABI.
 _bind("fp4b_version", _i, [])
 _bind("fp4b_gemm_tile_width", _i, [_i, _i, _i, _i])
+_bind("fp4b_selftest_bounded_wait", _i, [_i, _vp])
 _bind("fp4b_last_error", ctypes.c_char_p, [])
 _bind("fp4b_device_error", _i, [_i])
 _bind("fp4b_quantize", _i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp])

@@ -105,9 +105,19 @@ int fp4b_gemm_tile_width(int m, int n, int k, int sms);
 /* Message of the last failed call on this host thread ("" if none). */
 const char* fp4b_last_error(void);
 
-/* Non-zero if a kernel on the current device gave up on a bounded wait
- * (1 producer, 2 MMA, 3 epilogue); clear != 0 resets it.  Synchronises the device. */
+/* Non-zero if a kernel on the current device gave up on a bounded wait: the
+ * first code recorded (GEMM 1 producer, 2 MMA, 3 epilogue, 4 fused-quantize
+ * wait; 5 quantizer ring; 7 / 8 the self-test below); clear != 0 resets it.
+ * Synchronises the device. */
 int fp4b_device_error(int clear);
+
+/* Failure-path self-test (no counterpart in the reference, whose kernels do
+ * not wait): one block waits, with the bounded waits the kernels use, on an
+ * mbarrier phase nobody completes (which = 0) or a global word nobody writes
+ * (which = 1); after the 2 s bound the wait gives up, records 7 or 8 in the
+ * device error word and the kernel returns, leaving the context usable.
+ * Asynchronous on `stream`; 0, or -1 bad `which`, -4 launch failure. */
+int fp4b_selftest_bounded_wait(int which, void* stream);
 
 /* Quantize BF16 [rows, cols] (row stride ld elements) into caller buffers:
  * dst_fp4 [rows_pad, k_pad/2], dst_sf rows_pad*k_pad/16 bytes.  Positions
