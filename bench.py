@@ -16,12 +16,24 @@ every step on this GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Multi-GPU (torchrun, one rank per GPU): data-parallel M-split with weak
-scaling -- every rank runs the full per-GPU workload on its own activations,
-no collective on the data path; the reported value is all ranks' FLOPs over
-the slowest rank's time.  `--impl reference` times the reference's CPU path
-(its own quantizer compiled for the host + fp32 matmul of the dequantized
+Multi-GPU (torchrun, one rank per GPU): the headline is data-parallel with
+weak scaling -- every rank runs the full per-GPU workload on its own
+activations, no collective on the data path; the reported value is all ranks'
+FLOPs over the slowest rank's time.  The same line carries config 5 (the
+decoder-layer linear stack, M = 8192) run in every mode on the same ranks:
+"single" (each rank the whole stack alone: the 1-GPU time), "tp_p2p" and
+"tp_nccl" (weights N-sharded, output columns assembled on every rank by the
+GEMM epilogue's NVLink stores or by an NCCL all-gather), and "dp" (rows
+split), with strong-scaling efficiency, the bytes each rank receives per step
+and a byte-for-byte check of a column-parallel linear against one GPU
+(`tp_bytes_equal`).  `--impl reference` times the reference's CPU path (its
+own quantizer compiled for the host + fp32 matmul of the dequantized
 operands) on the host cores, on rank 0 only.
+
+Roofline denominator for the GEMM and the step: the larger of NVIDIA's dense
+NVFP4 figure (9 PFLOP/s) and the dense NVFP4 MMA rate measured in the same run
+by fp4b_mma_rate (`--config fp4peak` prints that measurement alone, with the
+GEMM mainloop's MMA mixes).
 """
 from __future__ import annotations
 
@@ -122,49 +134,6 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------ timing
-class L2Flusher:
-    """Evicts L2 (126 MB) before a timed step: writes one 256 MiB buffer, then
-    reads another, so the timed step starts cold and with no dirty lines whose
-    write-back would overlap it."""
-
-    def __init__(self, dev, mib: int = 256):
-        n = mib * 1024 * 1024 // 4
-        self.wbuf = torch.empty(n, dtype=torch.float32, device=dev)
-        self.rbuf = torch.ones(n, dtype=torch.float32, device=dev)
-        self.out = torch.empty((), dtype=torch.float32, device=dev)
-
-    def __call__(self):
-        self.wbuf.fill_(1.0)
-        torch.amax(self.rbuf, dim=0, out=self.out)
-
-
-def time_launches(fn, steps: int, warmup: int, flush=None, stream=None) -> list[float]:
-    """Per-call device milliseconds (CUDA events on `stream`), L2 flushed before each.
-
-    The GPU is first parked on a sleep kernel long enough for the host to
-    enqueue every timed call, so the events measure device time only, never a
-    gap in which the GPU waits for Python to launch the next kernel."""
-    stream = stream or torch.cuda.current_stream()
-    for _ in range(warmup):
-        if flush:
-            flush()
-        fn()
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        torch.cuda._sleep(int(2e6) * (steps + 10))  # ~1 ms of device time per step queued behind it
-    pairs = []
-    for _ in range(steps):
-        if flush:
-            flush()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        fn()
-        e.record(stream)
-        pairs.append((s, e))
-    torch.cuda.synchronize()
-    return [s.elapsed_time(e) for s, e in pairs]
-
-
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -287,7 +256,204 @@ def run_reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------ peak and roofline
+def measured_fp4_peak() -> dict | None:
+    """Dense NVFP4 MMA rate of this GPU (fp4b_mma_rate: N = 256, operands resident
+    in shared memory, no loads), or None when the measurement fails."""
+    import fp4_gemm
+    try:
+        return fp4_gemm.mma_rate(256, 0, False, 0, stages=8192, reps=5)
+    except RuntimeError:
+        return None
+
+
+def fp4_roofline_peak(measured: dict | None) -> tuple[float, str]:
+    """(denominator, its source): the larger of the 9 PF datasheet figure and the measured rate."""
+    if measured and measured["tflops"] > FP4_DATASHEET_TFLOPS:
+        return measured["tflops"], "dense NVFP4 MMA rate measured in this run (fp4b_mma_rate, N=256)"
+    return FP4_DATASHEET_TFLOPS, "NVIDIA B200 dense NVFP4 datasheet (9 PFLOP/s; above the rate measured in this run)"
+
+
+def roofline_entry(achieved: float, peak: float, peak_source: str, measured: dict | None, fp4_4x_bf16: float,
+                   **extra) -> dict:
+    d = {"bound": "tensor", **extra, "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+         "peak_source": peak_source, "frac_of_datasheet_9pf": achieved / FP4_DATASHEET_TFLOPS,
+         "frac_of_4x_measured_bf16": achieved / fp4_4x_bf16}
+    if measured:
+        d["frac_of_measured_mma_peak"] = achieved / measured["tflops"]
+    return d
+
+
+# ------------------------------------------------------------------------------ config 5: decoder stack
+STACK_LINEARS = (("qkv", 5120, 2880), ("o", 2880, 4096), ("gate_up", 15360, 2880), ("down", 2880, 7680))
+STACK_M = 8192
+
+
+def stack_flops(layers: int) -> float:
+    return 2.0 * STACK_M * layers * sum(n * k for _, n, k in STACK_LINEARS)
+
+
+def stack_weight(layer: int, j: int, dev) -> torch.Tensor:
+    """Weight of linear j of a layer: N(0, 0.02) BF16, from a seed of its own
+    (the same bytes on every rank and every GPU)."""
+    _, n, k = STACK_LINEARS[j]
+    g = torch.Generator(device=dev).manual_seed(1000 * layer + j)
+    return (torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+
+
+def stack_activations(dev, r0: int, r1: int) -> dict:
+    """Fresh N(0,1) activations per input width (the stack's shapes do not chain); rows [r0, r1)."""
+    g = torch.Generator(device=dev).manual_seed(7)
+    return {k: torch.randn(STACK_M, k, generator=g, device=dev).to(torch.bfloat16)[r0:r1].contiguous()
+            for k in sorted({k for _, _, k in STACK_LINEARS})}
+
+
+def time_stack(mode: str, layers: int, steps: int, warmup: int, ws: int, rank: int, dev) -> float:
+    """Milliseconds per stack step (max over ranks).  mode: "single" (this rank
+    runs the whole stack alone), "dp" (rows split over the ranks), "tp_p2p" /
+    "tp_nccl" (weights N-sharded, output columns assembled on every rank)."""
+    import torch.distributed as dist
+
+    import fp4_gemm
+    import fp4_gemm_dist as D
+    r0, r1 = D.row_range(STACK_M, ws, rank) if mode == "dp" else (0, STACK_M)
+    mods = []
+    for li in range(layers):
+        lin = []
+        for j in range(len(STACK_LINEARS)):
+            w = stack_weight(li, j, dev)
+            if mode.startswith("tp"):
+                lin.append(D.ColumnParallelFP4Linear(w, None, mode=mode[3:]))
+            else:
+                lin.append(fp4_gemm.FP4WeightCache(w))
+            del w
+        mods.append(lin)
+    xs = stack_activations(dev, r0, r1)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for lin in mods:
+            for mod, (_, _, k) in zip(lin, STACK_LINEARS):
+                if mode.startswith("tp"):
+                    mod.forward(xs[k])
+                else:
+                    mod.forward(xs[k], sync=False)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    if ws > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    for lin in mods:
+        for mod in lin:
+            mod.free()
+    del mods, xs
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    return ms
+
+
+def stack_recv_bytes(ws: int, layers: int) -> int:
+    """Bytes of output columns the busiest receiver takes in per tensor-parallel step."""
+    import fp4_gemm_dist as D
+    total = 0
+    for _, n, _ in STACK_LINEARS:
+        shards = D.plan_column_shards(n, ws)
+        total += STACK_M * (n - min(s.cols for s in shards)) * 2
+    return total * layers
+
+
+def tp_bytes_equal(ws: int, dev) -> bool:
+    """One column-parallel linear (the stack's QKV shape, 2048 rows, BF16 bias),
+    in both assembly modes, equals the single-GPU cache byte for byte on every rank."""
+    import torch.distributed as dist
+
+    import fp4_gemm
+    import fp4_gemm_dist as D
+    w = stack_weight(0, 0, dev)
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn(2048, w.shape[1], generator=g, device=dev).to(torch.bfloat16)
+    b = (torch.randn(w.shape[0], generator=g, device=dev) * 0.01).to(torch.bfloat16)
+    single = fp4_gemm.FP4WeightCache(w, b)
+    ref = single.forward(x, sync=True)
+    ok = True
+    for mode in ("p2p", "nccl"):
+        tp = D.ColumnParallelFP4Linear(w, b, mode=mode)
+        ok = ok and bool(torch.equal(tp.forward(x), ref))
+        tp.free()
+    single.free()
+    flag = torch.tensor([1 if ok else 0], device=dev, dtype=torch.int32)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    return bool(flag.item())
+
+
+def stack_report(args, ws: int, rank: int, dev) -> dict:
+    """Config 5 in every mode that applies at this world size (see the module docstring)."""
+    layers = args.layers
+    flops = stack_flops(layers)
+    modes = ["single"] + (["tp_p2p", "tp_nccl", "dp"] if ws > 1 else [])
+    out = {"workload": f"config 5: {layers} layers x (QKV 2880->5120, O 4096->2880, gate_up 2880->15360, "
+                       f"down 7680->2880), M={STACK_M} tokens, weights N(0,0.02) cached as NVFP4, fresh N(0,1) "
+                       "activations per linear (quantized every call), no bias",
+           "tflop_per_step": flops / 1e12, "steps": args.steps, "warmup": args.warmup, "modes": {}}
+    t_single = None
+    for mode in modes:
+        ms = time_stack(mode, layers, args.steps, args.warmup, ws, rank, dev)
+        entry = {"ms_per_step": ms}
+        if mode == "single":
+            t_single = ms
+            entry["tflops"] = flops / (ms * 1e-3) / 1e12
+            entry["note"] = "every rank runs the whole stack on its own GPU; the 1-GPU time (max over ranks)"
+        else:
+            entry["tflops"] = flops / (ms * 1e-3) / 1e12
+            entry["efficiency_vs_1gpu"] = t_single / (ws * ms)
+            if mode.startswith("tp"):
+                rb = stack_recv_bytes(ws, layers)
+                entry["recv_bytes_per_step_per_rank"] = rb
+                entry["nvlink_gbs_per_rank"] = rb / (ms * 1e-3) / 1e9
+        out["modes"][mode] = entry
+    if ws > 1:
+        out["tp_bytes_equal"] = tp_bytes_equal(ws, dev)
+    return out
+
+
 # ------------------------------------------------------------------------------ our arm
+def headline_sets(m, n, k, rank, dev):
+    import fp4_gemm
+    from tests import workloads as W
+    per_set = m * k * 2 + (n + 64) * k * 9 // 16 + m * n * 2 + m * k * 9 // 16
+    nsets = sets_needed(per_set)
+    sets = []
+    for i in range(nsets):
+        x, w, b = W.cached_linear_inputs(m, n, k, seed=1000 * rank + i)
+        xd, bd = x.to(dev), b.to(dev)
+        cache = fp4_gemm.FP4WeightCache(w.to(dev), bd)
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        aq, asf = fp4_gemm.quantize_to_buffers(xd, None, cache.K)
+        sets.append(dict(x=xd, b=bd, cache=cache, out=out, aq=aq, asf=asf, wsd=cache.state_dict()))
+    return sets, per_set
+
+
+def gemm_fn(lib, st, m, n, sptr):
+    kp = st["cache"].K
+    return lambda: lib.fp4b_gemm_prequant(st["aq"].data_ptr(), st["asf"].data_ptr(), m, st["aq"].shape[0],
+                                          st["wsd"]["fp4"].data_ptr(), st["wsd"]["sf"].data_ptr(), n,
+                                          st["cache"].N, kp, None, 0, st["out"].data_ptr(), n,
+                                          st["b"].data_ptr(), 1.0, 0.0, sptr)
+
+
 def run_ours(args):
     import datetime
 
@@ -304,23 +470,19 @@ def run_ours(args):
     dev = torch.device("cuda", local if ws > 1 else 0)
     torch.cuda.set_device(dev)
     peaks = load_peaks()
-    fp4_peak = 4.0 * peaks["bf16_tflops"]
+    fp4_4x_bf16 = 4.0 * peaks["bf16_tflops"]
     lib = fp4_gemm._lib
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
+    clocks = ClockSampler(dev.index if ws == 1 else local)
+    clocks.start()
+    mma_peak = measured_fp4_peak()
+    fp4_peak, fp4_peak_source = fp4_roofline_peak(mma_peak)
 
     # --- headline: cached linear 2048 x 2880 x 7680 + bias, buffer sets rotated past L2
     m, n, k = W.HEADLINE_SHAPE
-    per_set = m * k * 2 + (n + 64) * k * 9 // 16 + m * n * 2 + m * k * 9 // 16
-    nsets = sets_needed(per_set)
-    sets = []
-    for i in range(nsets):
-        x, w, b = W.cached_linear_inputs(m, n, k, seed=1000 * rank + i)
-        xd, bd = x.to(dev), b.to(dev)
-        cache = fp4_gemm.FP4WeightCache(w.to(dev), bd)
-        out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
-        aq, asf = fp4_gemm.quantize_to_buffers(xd, None, cache.K)
-        sets.append(dict(x=xd, b=bd, cache=cache, out=out, aq=aq, asf=asf, wsd=cache.state_dict()))
+    sets, per_set = headline_sets(m, n, k, rank, dev)
+    nsets = len(sets)
 
     def make_step(st):
         def step():
@@ -330,21 +492,12 @@ def run_ours(args):
                 raise RuntimeError(f"cached linear failed: {rc} {fp4_gemm._last_error()}")
         return step
 
-    def make_gemm(st):
-        kp = st["cache"].K
-        return lambda: lib.fp4b_gemm_prequant(st["aq"].data_ptr(), st["asf"].data_ptr(), m, st["aq"].shape[0],
-                                              st["wsd"]["fp4"].data_ptr(), st["wsd"]["sf"].data_ptr(), n,
-                                              st["cache"].N, kp, None, 0, st["out"].data_ptr(), n,
-                                              st["b"].data_ptr(), 1.0, 0.0, sptr)
-
     def make_quant(st):
         kp = st["cache"].K
         return lambda: lib.fp4b_quantize(st["x"].data_ptr(), m, k, k, st["aq"].data_ptr(), st["asf"].data_ptr(),
                                          st["aq"].shape[0], kp, sptr)
 
     steps_fns = [make_step(st) for st in sets]
-    clocks = ClockSampler(dev.index if ws == 1 else local)
-    clocks.start()
     if ws > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -352,9 +505,8 @@ def run_ours(args):
     torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
-    gemm_ms = time_rotating([make_gemm(st) for st in sets], args.steps, args.warmup, stream)
+    gemm_ms = time_rotating([gemm_fn(lib, st, m, n, sptr) for st in sets], args.steps, args.warmup, stream)
     quant_ms = time_rotating([make_quant(st) for st in sets], args.steps, args.warmup, stream)
-    clk = clocks.stop()
 
     if ws > 1:
         t = torch.tensor([ms_per_step], device=dev, dtype=torch.float64)
@@ -363,8 +515,13 @@ def run_ours(args):
     flops = 2.0 * m * n * k
     value = ws * flops / (ms_per_step * 1e-3) / 1e12
     gemm_tflops = flops / (gemm_ms * 1e-3) / 1e12
+    step_tflops = flops / (ms_per_step * 1e-3) / 1e12
     aq0 = sets[0]["aq"]
     quant_bytes = m * k * 2 + aq0.shape[0] * aq0.shape[1] + aq0.shape[0] * aq0.shape[1] // 8
+    tile = fp4_gemm.gemm_tile_width(m, n, k, torch.cuda.get_device_properties(dev).multi_processor_count)
+
+    # --- config 5 on every rank (all modes that apply at this world size)
+    stack = stack_report(args, ws, rank, dev)
 
     result = None
     if rank == 0:
@@ -414,9 +571,8 @@ def run_ours(args):
                 if rc != 0:
                     raise RuntimeError(f"dynamic matmul failed: {rc} {fp4_gemm._last_error()}")
             dms = time_rotating([dyn], max(3, args.steps // 10), 3, stream)
-            dynamic[f"{dn}^3"] = {"ms": dms, "tflops": 2.0 * dn ** 3 / (dms * 1e-3) / 1e12,
-                                  "pct_fp4_peak_4x_measured_bf16": 100.0 * 2.0 * dn ** 3 / (dms * 1e-3) / 1e12
-                                  / fp4_peak}
+            dtf = 2.0 * dn ** 3 / (dms * 1e-3) / 1e12
+            dynamic[f"{dn}^3"] = {"ms": dms, "tflops": dtf, "frac_of_roofline_peak": dtf / fp4_peak}
             del da, db, dd
 
         # end to end through the public API: pinned host in, pinned host out, every step
@@ -428,7 +584,9 @@ def run_ours(args):
         def e2e_step():
             cache0.forward_host(x_host, out=y_host)
         e2e_ms = time_rotating([e2e_step], args.steps, args.warmup, stream)
+    clk = clocks.stop()
 
+    if rank == 0:
         cpu = cpu_baseline(m, n, k) if ws == 1 else None
         traffic = None
         tp = os.path.join(ROOT, "profiles", "roofline_traffic.json")
@@ -454,23 +612,27 @@ def run_ours(args):
                        "l2": f"inputs larger than L2: {nsets} independent input/weight/output sets rotated "
                              f"({nsets * per_set / 2**20:.0f} MiB per pass), K steps back to back"},
             "pct_fp4_peak_datasheet": 100.0 * (value / ws) / FP4_DATASHEET_TFLOPS,
-            "pct_fp4_peak_4x_measured_bf16": 100.0 * (value / ws) / fp4_peak,
+            "pct_fp4_peak_4x_measured_bf16": 100.0 * (value / ws) / fp4_4x_bf16,
+            "measured_mma_peak": mma_peak,
             "kernels": {"quantize_activations_us": quant_ms * 1e3, "gemm_us": gemm_ms * 1e3,
                         "step_us": ms_per_step * 1e3,
-                        "quantize_activations_gbs": quant_bytes / (quant_ms * 1e-3) / 1e9},
-            "roofline": {"bound": "tensor", "kernel": "nvf4_gemm_pair_kernel (2048x2880x7680, 256x320 CTA-pair tiles, N = 128 + 192 MMAs per k-block)",
-                         "achieved": gemm_tflops, "peak": fp4_peak, "unit": "TFLOP/s",
-                         "frac": gemm_tflops / fp4_peak, "traffic": traffic,
-                         "peak_source": f"4 x bf16 dense burst ({peaks['source']}, MEASURED_PEAKS.json): "
-                                        "B200 dense FP4 = 4 x dense BF16",
-                         "frac_of_datasheet_9pf": gemm_tflops / FP4_DATASHEET_TFLOPS},
+                        "quantize_activations_gbs": quant_bytes / (quant_ms * 1e-3) / 1e9,
+                        "quantize_activations_frac_hbm": quant_bytes / (quant_ms * 1e-3) / 1e9 / peaks["hbm_gbs"]},
+            "roofline": roofline_entry(
+                gemm_tflops, fp4_peak, fp4_peak_source, mma_peak, fp4_4x_bf16,
+                kernel=f"nvf4_gemm_pair_kernel (2048x2880x7680, {tile}-wide CTA-pair tiles)", traffic=traffic),
+            "roofline_step": roofline_entry(
+                step_tflops, fp4_peak, fp4_peak_source, mma_peak, fp4_4x_bf16,
+                what="whole cached-linear step: activation quantize + GEMM + fused bias, per GPU"),
             "quantize": {"workload": "config 4: 16384x16384 bf16 Student-t stress, bit-exact",
                          "value": q4_gbs, "unit": "GB/s", "ms": q4_ms,
                          "roofline": {"bound": "hbm", "achieved": q4_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                                      "frac": q4_gbs / peaks["hbm_gbs"], "algorithmic_bytes": q4_bytes}},
+                                      "frac": q4_gbs / peaks["hbm_gbs"], "algorithmic_bytes": q4_bytes,
+                                      "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peaks['source']})"}},
             "sweep": sweep,
             "dynamic": {"workload": "config 3: fp4_matmul path (quantize A and B, GEMM) per call, N(0,1) operands, "
                                     "inputs larger than L2", **dynamic},
+            "stack": stack,
             "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
                     "h2d_bytes_per_step": m * k * 2, "d2h_bytes_per_step": m * n * 2,
                     "path": "fp4_gemm.FP4WeightCache.forward_host(pinned x, out=pinned y): 512-row chunks, "
@@ -489,89 +651,24 @@ def run_ours(args):
         print(json.dumps(result), flush=True)
 
 
-# ------------------------------------------------------------------------------ config 5: decoder stack
-STACK_LINEARS = (("qkv", 5120, 2880), ("o", 2880, 4096), ("gate_up", 15360, 2880), ("down", 2880, 7680))
-
-
 def run_stack(args):
-    """Config 5: 12 decoder layers x {QKV 2880->5120, O 4096->2880, gate_up
-    2880->15360, down 7680->2880} on M=8192 tokens, weights N(0,0.02) cached
-    as NVFP4, activations N(0,1) fed fresh to every linear (the shapes do not
-    chain).  tp: every linear column-parallel over the ranks, output
-    assembled on every rank (--tp-mode p2p: the GEMM epilogue stores into all
-    ranks' buffers; nccl: all-gather).  dp: the 8192 rows split over the
-    ranks, weights replicated, no collective."""
+    """Config 5 alone (`--config stack`): every mode that applies at this world size, one JSON line."""
     import datetime
 
     import torch.distributed as dist
-
-    import fp4_gemm
-    import fp4_gemm_dist as D
 
     ws, rank, local = dist_env()
     dev = torch.device("cuda", local if ws > 1 else 0)
     torch.cuda.set_device(dev)
     if ws > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
-    m_total = 8192
-    r0, r1 = D.row_range(m_total, ws, rank) if args.stack_mode == "dp" else (0, m_total)
-    m = r1 - r0
-    layers = []
-    g = torch.Generator(device=dev)
-    for li in range(args.layers):
-        lin = []
-        for j, (name, n, k) in enumerate(STACK_LINEARS):
-            g.manual_seed(1000 * li + j)
-            w = (torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-            if args.stack_mode == "tp" and ws > 1:
-                lin.append(D.ColumnParallelFP4Linear(w, None, mode=args.tp_mode))
-            else:
-                lin.append(fp4_gemm.FP4WeightCache(w))
-            del w
-        layers.append(lin)
-    g.manual_seed(7)
-    xs = {k: torch.randn(m_total, k, generator=g, device=dev).to(torch.bfloat16)[r0:r1]
-          for k in sorted({k for _, _, k in STACK_LINEARS})}
-    stream = torch.cuda.current_stream(dev)
-
-    def step():
-        for lin in layers:
-            for mod, (_, _, k) in zip(lin, STACK_LINEARS):
-                if isinstance(mod, D.ColumnParallelFP4Linear):
-                    mod.forward(xs[k])
-                else:
-                    mod.forward(xs[k], sync=False)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if ws > 1:
-        dist.barrier()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    for _ in range(args.steps):
-        step()
-    b.record(stream)
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / args.steps
-    if ws > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    flops = 2.0 * m_total * args.layers * sum(n * k for _, n, k in STACK_LINEARS)
+    rep = stack_report(args, ws, rank, dev)
     if rank == 0:
-        par = (f"tp{ws} ({args.tp_mode})" if args.stack_mode == "tp" and ws > 1 else
-               f"dp{ws} (M-split, no collective)")
-        print(json.dumps({
-            "metric": "decoder-stack TFLOPS (config 5)", "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOPS",
-            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong", "dtype": "nvfp4", "data": "synthetic",
-            "config": {"workload": f"{args.layers} layers x (QKV 2880->5120, O 4096->2880, gate_up 2880->15360, "
-                                   f"down 7680->2880), M={m_total} tokens, fresh activations per linear",
-                       "parallelism": par, "tflop_per_step": flops / 1e12}}), flush=True)
-    for lin in layers:
-        for mod in lin:
-            mod.free()
+        best = max(rep["modes"].values(), key=lambda e: e["tflops"])
+        print(json.dumps({"metric": "decoder-stack TFLOPS (config 5)", "value": best["tflops"], "unit": "TFLOPS",
+                          "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": best["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+                          "dtype": "nvfp4", "data": "synthetic", "stack": rep}), flush=True)
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -615,17 +712,76 @@ def run_quantize(args):
                       "gpu_launches": args.steps}), flush=True)
 
 
+def run_gemm(args):
+    """The headline GEMM alone (`--config gemm`): 2048 x 2880 x 7680 + bias on
+    operands quantized beforehand, buffer sets rotated past L2, one JSON line.
+    The command the GEMM's ncu captures run (one kernel per step, nothing else
+    in the timed loop)."""
+    import fp4_gemm
+    from tests import workloads as W
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = fp4_gemm._lib
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+    m, n, k = W.HEADLINE_SHAPE
+    sets, per_set = headline_sets(m, n, k, 0, dev)
+    ms = time_rotating([gemm_fn(lib, st, m, n, sptr) for st in sets], args.steps, args.warmup, stream)
+    tflops = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+    tile = fp4_gemm.gemm_tile_width(m, n, k, torch.cuda.get_device_properties(dev).multi_processor_count)
+    print(json.dumps({"metric": "headline GEMM TFLOPS (2048x2880x7680 + bias, operands pre-quantized)",
+                      "value": tflops, "unit": "TFLOPS", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": ms, "higher_is_better": True, "dtype": "nvfp4", "data": "synthetic",
+                      "config": {"workload": f"GEMM {m}x{n}x{k} + bias, {tile}-wide CTA-pair tiles",
+                                 "l2": f"{len(sets)} buffer sets rotated ({len(sets) * per_set / 2**20:.0f} MiB)"},
+                      "frac_of_datasheet_9pf": tflops / FP4_DATASHEET_TFLOPS,
+                      "gpu_launches": args.steps}), flush=True)
+    for st in sets:
+        st["cache"].free()
+
+
+# (n0, n1, scale copies, scale-B atoms per k-block): the dense peak, then the
+# per-k-block MMA work of the GEMM's tile widths with and without their
+# scale copies.
+MMA_MIXES = [(256, 0, False, 0), (128, 0, False, 0), (192, 0, False, 0), (128, 192, False, 0),
+             (192, 192, False, 0), (128, 0, True, 1), (192, 0, True, 2), (256, 0, True, 2), (128, 192, True, 3),
+             (192, 192, True, 3), (128, 192, True, 2)]
+
+
+def run_fp4peak(args):
+    """`--config fp4peak`: the dense NVFP4 MMA rate of this GPU (the GEMM
+    roofline's measured denominator) and the tensor-pipe rate of the GEMM
+    mainloop's MMA mixes, operands resident in shared memory (no loads)."""
+    import fp4_gemm
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    clocks = ClockSampler(0)
+    clocks.start()
+    mixes = {}
+    for n0, n1, cp, atoms in MMA_MIXES:
+        r = fp4_gemm.mma_rate(n0, n1, cp, atoms, stages=8192, reps=3)
+        key = f"N={n0}" + (f"+{n1}" if n1 else "") + (f", {1 + atoms} scale copies per k-block" if cp else "")
+        mixes[key] = {"tflops": r["tflops"], "ms": r["ms"], "pairs": r["pairs"]}
+    clk = clocks.stop()
+    peak = mixes["N=256"]["tflops"]
+    print(json.dumps({"metric": "dense NVFP4 MMA rate (tcgen05.mma.cta_group::2.kind::mxf4nvf4.block16, M=256, "
+                                "K=64, operands resident in shared memory)",
+                      "value": peak, "unit": "TFLOP/s", "n_gpus": 1, "higher_is_better": True,
+                      "frac_of_datasheet_9pf": peak / FP4_DATASHEET_TFLOPS, "mixes": mixes,
+                      "gpu_launches": 4 * len(MMA_MIXES), "clocks": clk}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["headline", "stack", "quantize"], default="headline",
-                    help="stack: config 5 decoder-layer linear stack; quantize: config 4 quantizer alone "
-                         "(neither is the headline metric)")
-    ap.add_argument("--stack-mode", choices=["tp", "dp"], default="tp")
-    ap.add_argument("--tp-mode", choices=["p2p", "nccl"], default="p2p")
+    ap.add_argument("--config", choices=["headline", "stack", "quantize", "gemm", "fp4peak"], default="headline",
+                    help="stack: config 5 decoder-layer linear stack; quantize: config 4 quantizer alone; gemm: "
+                         "the headline GEMM alone; fp4peak: the measured NVFP4 MMA rate (none of these is the "
+                         "headline metric)")
     ap.add_argument("--layers", type=int, default=12)
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -633,6 +789,10 @@ def main():
         run_stack(args)
     elif args.config == "quantize":
         run_quantize(args)
+    elif args.config == "gemm":
+        run_gemm(args)
+    elif args.config == "fp4peak":
+        run_fp4peak(args)
     elif args.impl == "reference":
         run_reference_arm(args)
     else:

@@ -11,6 +11,7 @@
 
 #include <cmath>
 #include <cstdarg>
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -154,13 +155,6 @@ int init_locked(DeviceState& s, int M, int N, int K) {
     return 0;
 }
 
-int launch_status(cudaError_t e, const char* what) {
-    if (e == cudaSuccess) return 0;
-    set_last_error("%s: %s", what, cudaGetErrorString(e));
-    fprintf(stderr, "fp4_gemm: %s: %s\n", what, cudaGetErrorString(e));
-    return -4;
-}
-
 int quantize_into(const void* src, long rows, long cols, long ld, uint8_t* fp4, uint8_t* sf, long rows_pad,
                   long k_pad, cudaStream_t st) {
     QuantizeArgs q{src, rows, cols, ld, rows_pad, k_pad, fp4, sf};
@@ -180,6 +174,13 @@ int gemm_into(const GemmArgs& g, cudaStream_t st) {
 }
 
 }  // namespace
+
+int launch_status(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return 0;
+    set_last_error("%s: %s", what, cudaGetErrorString(e));
+    fprintf(stderr, "fp4_gemm: %s: %s\n", what, cudaGetErrorString(e));
+    return -4;
+}
 
 int* device_error_word() {
     const int d = current_device();
@@ -375,6 +376,20 @@ FP4B_EXPORT int fp4b_run_cached_ex(const void* A, int m, int k_in, int lda, cons
 FP4B_EXPORT int fp4b_run_cached_peers(const void* A, int m, int k_in, int lda, const void* h, int n_out,
                                       void* D, int ldd, void* const* peer_d, int npeers, const void* bias,
                                       void* stream) {
+    // The epilogue writes D and every peer buffer with 16-byte stores (TMA for
+    // D, plain vector stores over NVLink for the peers): a misaligned peer
+    // address or row stride would fault on the GPU, so it is refused here,
+    // before anything is looked up or launched.
+    if (peer_d && npeers >= 1 && npeers <= 7) {
+        bool aligned = ldd % 8 == 0 && (reinterpret_cast<uintptr_t>(D) & 15) == 0;
+        for (int i = 0; i < npeers && aligned; ++i)
+            aligned = peer_d[i] && (reinterpret_cast<uintptr_t>(peer_d[i]) & 15) == 0;
+        if (!aligned) {
+            set_last_error("fp4b_run_cached_peers: D, every peer_d[i] and ldd must give 16-byte aligned rows "
+                           "(addresses multiples of 16 bytes, ldd a multiple of 8 elements, no NULL peer)");
+            return -2;
+        }
+    }
     WeightCache* c = as_cache(h);
     if (!c) {
         set_last_error("null or invalid cache handle");
@@ -400,7 +415,7 @@ FP4B_EXPORT int fp4b_run_cached_peers(const void* A, int m, int k_in, int lda, c
     g.b_cached = true;
     const cudaError_t e = gemm_launch_peers(g, peer_d, npeers, st);
     if (e == cudaErrorNotSupported) {
-        set_last_error("fp4b_run_cached_peers: needs 16-byte aligned output rows");
+        set_last_error("fp4b_run_cached_peers: the output tensor map could not be built for D");
         return -2;
     }
     return launch_status(e, "peer gemm launch");

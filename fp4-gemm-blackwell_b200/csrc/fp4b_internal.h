@@ -87,4 +87,9 @@ int read_and_clear_device_error();
 // Per-thread message of the last failure in the C ABI.
 void set_last_error(const char* fmt, ...);
 
+// 0 for cudaSuccess; otherwise records "<what>: <CUDA error>" as the last
+// error, prints it to stderr like the reference's messages, and returns -4
+// (the C ABI's launch-failure code).
+int launch_status(cudaError_t e, const char* what);
+
 }  // namespace fp4b

@@ -95,31 +95,24 @@ FP4B_EXPORT int fp4b_run_cached_noalloc(const void* A, int m, int k_in, int lda,
     }
     int dev = 0;
     uint8_t* scratch = scratch_for_current_device(&dev);
-    if (!scratch) return -4;
+    if (!scratch) return -1;  // the scratch is unavailable, as an allocation failure is in fp4b_run_cached_ex
     uint8_t* a_fp4 = scratch;
     uint8_t* a_sf = scratch + kNoallocFp4Bytes;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
 
     QuantizeArgs q{A, m, k_in, lda, m_pad, c.K, a_fp4, a_sf};
-    if (const char* why = quantize_check(q)) {
-        set_last_error("fp4b_run_cached_noalloc: %s", why);
-        return -1;
-    }
-    cudaError_t e = quantize_launch(q, st);
-    if (e != cudaSuccess) {
-        set_last_error("fp4b_run_cached_noalloc: quantize launch: %s", cudaGetErrorString(e));
-        return -4;
-    }
     GemmArgs g{a_fp4, a_sf, c.fp4, c.sf, m, n_out, c.K, m_pad, c.N, C, ldc, D, ldd, bias, alpha * c.w_alpha, beta};
+    // Geometry the kernels cannot take: -2 ("cannot implement"), checked for
+    // both kernels before either is launched.
+    if (const char* why = quantize_check(q)) {
+        set_last_error("fp4b_run_cached_noalloc: quantize: %s", why);
+        return -2;
+    }
     if (const char* why = gemm_check(g)) {
-        set_last_error("fp4b_run_cached_noalloc: %s", why);
-        return -1;
+        set_last_error("fp4b_run_cached_noalloc: gemm: %s", why);
+        return -2;
     }
+    if (int rc = launch_status(quantize_launch(q, st), "fp4b_run_cached_noalloc: quantize launch")) return rc;
     g.b_cached = true;  // right behind the activation quantizer
-    e = gemm_launch(g, st);
-    if (e != cudaSuccess) {
-        set_last_error("fp4b_run_cached_noalloc: gemm launch: %s", cudaGetErrorString(e));
-        return -4;
-    }
-    return 0;
+    return launch_status(gemm_launch(g, st), "fp4b_run_cached_noalloc: gemm launch");
 }

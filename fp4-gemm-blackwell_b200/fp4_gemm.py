@@ -81,6 +81,7 @@ _bind("fp4b_run_cached_peers", _i, [_vp, _i, _i, _i, _vp, _i, _vp, _i, ctypes.PO
 _bind("fp4b_ipc_get_handle", _i, [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_long)])
 _bind("fp4b_ipc_open_handle", _vp, [ctypes.c_char_p, ctypes.c_long])
 _bind("fp4b_ipc_close", _i, [_vp, ctypes.c_long])
+_bind("fp4b_mma_rate", _i, [_i, _i, _i, _i, _i, ctypes.POINTER(_i), _vp])
 
 # Query scale factor vector size
 SF_VEC_SIZE = _lib.fp4_gemm_sf_vec_size()
@@ -113,8 +114,8 @@ def global_weight_scale(amax: float) -> float:
 
 
 def _pad_to_multiple(x: int, m: int) -> int:
-    """Round up x to the nearest multiple of m."""
-    return ((x + m - 1) // m) * m
+    """Smallest multiple of m that is >= x (the reference pads M, N, K to 128)."""
+    return -(-x // m) * m
 
 
 def _stream_ptr(device) -> int:
@@ -142,23 +143,20 @@ def fp4_matmul(
     beta: float = 0.0,
 ) -> torch.Tensor:
     """
-    FP4 matrix multiply on B200 tensor cores.
+    Dynamic NVFP4 product: both operands are quantized on every call.
 
-    Computes: D = alpha * quantize_fp4(A) @ quantize_fp4(B)^T + beta * C
+    D = alpha * q(A) @ q(B)^T + beta * C, where q() is the NVFP4 quantizer
+    (E2M1 values, one UE4M3 scale per 16 elements along K) and the product is
+    accumulated in fp32 by the tcgen05 tensor cores and rounded to BF16.
 
-    Args:
-        A: Input activation tensor [M, K] or [batch, M, K], BF16 on CUDA
-        B: Weight tensor [N, K], BF16 on CUDA
-        C: Optional bias/residual tensor [M, N], BF16 on CUDA
-        alpha: Scalar multiplier for GEMM result
-        beta: Scalar multiplier for C
+    A is [M, K] or a batch [b, M, K] of activations, B is [N, K] (a weight in
+    F.linear layout), C an optional [M, N] term scaled by beta; all BF16 CUDA
+    tensors (other float types are cast to BF16 first).  The result is a BF16
+    [M, N] tensor, or [b, M, N] for a batched A.
 
-    Returns:
-        D: Output tensor [M, N] or [batch, M, N], BF16 on CUDA
-
-    Any M, N, K are accepted (the quantized operands are zero-padded to
-    multiples of 128 exactly as the reference pads them).  Synchronises the
-    device before returning, like the reference's fp4_gemm_run.
+    M, N and K need not be multiples of 128: the quantized operands equal the
+    reference's zero-padded ones, without the padding copies.  The device is
+    synchronised before returning, as the reference's fp4_gemm_run does.
     """
     batched = A.dim() == 3
     if batched:
@@ -209,15 +207,11 @@ def fp4_matmul(
 
 def fp4_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor = None) -> torch.Tensor:
     """
-    Drop-in replacement for F.linear using FP4 tensor cores.
+    F.linear(x, weight, bias) computed as a dynamic NVFP4 product.
 
-    Args:
-        x: Input tensor [..., K], BF16 on CUDA
-        weight: Weight tensor [N, K], BF16 on CUDA
-        bias: Optional bias [N], BF16 on CUDA
-
-    Returns:
-        Output tensor [..., N]
+    x is [..., K]; weight is [N, K]; bias, when given, is [N] and is added to
+    the BF16 product afterwards (a second BF16 rounding, as in the reference).
+    Returns [..., N].
     """
     orig_shape = x.shape
     x_2d = x.reshape(-1, x.shape[-1])
@@ -232,68 +226,50 @@ def fp4_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor = None)
 
 
 def sync():
-    """Synchronize the device. Call after pipelined FP4 operations."""
+    """Wait for all queued work on the current device (cudaDeviceSynchronize);
+    use it after a run of forward(..., sync=False) calls."""
     _lib.fp4_gemm_sync()
 
 
 def prealloc(max_M: int, max_N: int, max_K: int):
     """
-    Pre-allocate internal buffers for the maximum expected dimensions.
-    Call once before inference to avoid reallocation during forward passes.
-
-    Args:
-        max_M: Maximum M dimension (batch_size * seq_len, rounded to 128)
-        max_N: Maximum N dimension across all weight matrices
-        max_K: Maximum K dimension across all weight matrices
+    Size the library's per-device scratch for the largest problem to come
+    (rows of activations, output features, input features; each rounded up to
+    128 here), so that later calls do not grow it while a model is running.
     """
-    max_M = _pad_to_multiple(max_M, 128)
-    max_N = _pad_to_multiple(max_N, 128)
-    max_K = _pad_to_multiple(max_K, 128)
-    rc = _lib.fp4_gemm_prealloc(max_M, max_N, max_K)
+    rc = _lib.fp4_gemm_prealloc(*(_pad_to_multiple(v, 128) for v in (max_M, max_N, max_K)))
     if rc != 0:
         raise RuntimeError(f"fp4_gemm_prealloc failed with code {rc}")
 
 
 def cleanup():
-    """Release CUDA memory held by the FP4 GEMM library."""
+    """Free the scratch buffers the library holds on the current device."""
     _lib.fp4_gemm_cleanup()
 
 
 class FP4WeightCache:
     """
-    Cached FP4 weights for fast inference.
+    A weight quantized to NVFP4 once and kept on the GPU.
 
-    Quantizes BF16 weights to NVFP4 format once, then reuses the
-    pre-quantized data for every GEMM call. Only activations get
-    quantized on the fly.
+    Each ``forward(x)`` quantizes only the activations and multiplies them
+    with the stored weight (plus the bias, when one was given).  Free the
+    device memory with ``free()``, or use the object in a ``with`` block.
 
-    Usage:
-        cache = FP4WeightCache(weight)  # quantize once
-        output = cache.forward(x)       # fast inference
-        cache.free()                    # release GPU memory
-
-    Or as a context manager:
-        with FP4WeightCache(weight) as cache:
-            output = cache.forward(x)
-
-    The device bytes (``fp4_bytes`` packed E2M1 of the [N, K] weight padded to
-    multiples of 128, then ``sf_bytes`` scales) are identical to the
-    reference's cache for the same weight.
+    The stored bytes (``fp4_bytes`` of packed E2M1 for the weight padded to
+    multiples of 128 in both dimensions, then ``sf_bytes`` of scales) are the
+    ones the reference's cache holds for the same weight.
     """
 
     def __init__(self, weight: torch.Tensor, bias: torch.Tensor = None, global_scale: bool = False):
         """
-        Quantize a weight matrix to FP4 and cache on device.
-
-        Args:
-            weight: [N, K] BF16 weight matrix on CUDA
-            bias: Optional [N] bias vector
-            global_scale: two-level NVFP4 (not in the reference; off by default,
-                which keeps the reference's bytes): cache weight * s with the
-                power of two s of ``global_weight_scale(|weight|max)``, and
-                multiply every GEMM with the cache by 1 / s.  Improves the
-                accuracy of small-magnitude weights (e.g. N(0, 0.02)), whose
-                block scales otherwise fall in UE4M3's truncated subnormals.
+        weight: the [N, K] CUDA weight (F.linear layout; cast to BF16).
+        bias: optional [N] tensor added to every output row.
+        global_scale: two-level NVFP4, not in the reference and off by default
+            (off keeps the reference's bytes).  The cache then holds
+            weight * s, s the power of two ``global_weight_scale(|weight|max)``,
+            and every GEMM with it is multiplied by 1 / s.  This helps weights
+            of small magnitude (e.g. N(0, 0.02)), whose block scales would
+            otherwise fall among UE4M3's truncated subnormals.
         """
         self._handle = None
         assert weight.dim() == 2, f"Weight must be 2D [N, K], got {weight.shape}"
@@ -349,14 +325,10 @@ class FP4WeightCache:
 
     def forward(self, x: torch.Tensor, sync: bool = True) -> torch.Tensor:
         """
-        Run FP4 GEMM: output = x @ cached_weight.T + bias
-
-        Args:
-            x: Input activation [..., K], BF16 on CUDA
-            sync: If True, synchronize after GEMM. Set False for pipelined calls.
-
-        Returns:
-            Output tensor [..., N]
+        y = q(x) @ W^T (+ bias) for activations x [..., K] on the cache's
+        device; returns [..., N].  The work is queued on the current stream;
+        with sync=True (the reference's default) the device is synchronised
+        before returning, so pass sync=False for back-to-back calls.
         """
         if self._handle is None:
             raise RuntimeError("FP4WeightCache has been freed")
@@ -543,7 +515,7 @@ class FP4WeightCache:
         return cls._from_handle(h, sd["N_orig"], sd["K_orig"], device, bias)
 
     def free(self):
-        """Release GPU memory for cached weights."""
+        """Free the cached weight's device memory (later forwards raise)."""
         if getattr(self, "_handle", None) and _lib is not None:
             _lib.fp4_weight_cache_free(ctypes.c_void_p(self._handle))
             self._handle = None
@@ -559,23 +531,13 @@ class FP4WeightCache:
         self.free()
 
     def __repr__(self):
-        status = "active" if self._handle else "freed"
-        mb = (self.fp4_bytes + self.sf_bytes) / (1024 * 1024)
-        return f"FP4WeightCache([{self.N_orig}, {self.K_orig}], {mb:.1f} MB, {status})"
+        size_mb = (self.fp4_bytes + self.sf_bytes) / 2 ** 20
+        state = "freed" if not self._handle else "active"
+        return "FP4WeightCache([%d, %d], %.1f MB, %s)" % (self.N_orig, self.K_orig, size_mb, state)
 
 
 def fp4_quantize(weight: torch.Tensor, bias: torch.Tensor = None, global_scale: bool = False) -> FP4WeightCache:
-    """
-    Quantize a weight matrix to FP4 and cache on device.
-
-    Args:
-        weight: [N, K] BF16 weight matrix on CUDA
-        bias: Optional [N] bias vector
-        global_scale: opt-in two-level NVFP4 (see FP4WeightCache)
-
-    Returns:
-        FP4WeightCache handle for fast inference
-    """
+    """Build an FP4WeightCache for `weight` (and `bias`); see that class."""
     return FP4WeightCache(weight, bias, global_scale=global_scale)
 
 
@@ -583,20 +545,8 @@ def fp4_cached_matmul(
     A: torch.Tensor,
     cache: FP4WeightCache,
 ) -> torch.Tensor:
-    """
-    FP4 matrix multiply with pre-quantized weights.
-
-    Computes: D = quantize_fp4(A) @ cached_B_fp4.T
-
-    Only A is quantized on the fly. B uses pre-quantized cache.
-
-    Args:
-        A: Input tensor [M, K] or [batch, M, K], BF16 on CUDA
-        cache: Pre-quantized weight cache from fp4_quantize()
-
-    Returns:
-        D: Output tensor [M, N] or [batch, M, N], BF16 on CUDA
-    """
+    """q(A) @ W^T with W stored in `cache` ([M, K] or [b, M, K] in, [.., N] out);
+    the same call as cache.forward(A)."""
     return cache.forward(A)
 
 
@@ -604,16 +554,8 @@ def fp4_cached_linear(
     x: torch.Tensor,
     cache: FP4WeightCache,
 ) -> torch.Tensor:
-    """
-    Drop-in replacement for F.linear using cached FP4 weights.
-
-    Args:
-        x: Input tensor [..., K], BF16 on CUDA
-        cache: Pre-quantized weight cache (includes bias if provided)
-
-    Returns:
-        Output tensor [..., N]
-    """
+    """F.linear(x, W, bias) with W (and its bias) stored in `cache`; x is [..., K],
+    the result [..., N]."""
     return cache.forward(x)
 
 
@@ -662,6 +604,32 @@ def gemm_tile_width(m: int, n: int, k: int, sms: int = 148) -> int:
     if w < 0:
         raise ValueError(f"gemm_tile_width: {_last_error()}")
     return w
+
+
+def mma_rate(n0: int = 256, n1: int = 0, sf_copies: bool = False, sfb_atoms: int = 0, stages: int = 8192,
+             reps: int = 5) -> dict:
+    """Measured tensor-pipe rate of the block-scaled MMA on the current device
+    (fp4b_mma_rate; operands resident in shared memory, no loads): the best of
+    `reps` CUDA-event-timed launches after one warm-up launch.  Returns
+    {"tflops", "ms", "pairs"}.  The defaults measure the dense NVFP4 peak."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(dev)
+    pairs = _i(0)
+    best = None
+    for rep in range(reps + 1):
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        rc = _lib.fp4b_mma_rate(n0, n1, 1 if sf_copies else 0, sfb_atoms, stages, ctypes.byref(pairs),
+                                stream.cuda_stream)
+        stop.record(stream)
+        if rc != 0:
+            raise RuntimeError(f"fp4b_mma_rate failed with error code {rc} ({_last_error()})")
+        stop.synchronize()
+        ms = start.elapsed_time(stop)
+        if rep > 0 and (best is None or ms < best):
+            best = ms
+    flops = pairs.value * stages * 4 * 2 * 256 * (n0 + n1) * 64
+    return {"tflops": flops / (best * 1e-3) / 1e12, "ms": best, "pairs": pairs.value}
 
 
 def device_error(clear: bool = True) -> int:

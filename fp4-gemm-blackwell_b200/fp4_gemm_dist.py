@@ -156,6 +156,13 @@ class ColumnParallelFP4Linear:
         import fp4_gemm
         if self._bufs is not None and self._bufs.shape[1] >= m:
             return
+        if self._bufs is not None:
+            # The host runs ahead of the GPU: this rank's previous GEMM may still be
+            # storing through the peer mappings.  Its stream, which also holds the
+            # previous call's rank-ordering step (after which every peer's stores
+            # into this rank's old buffer are done), must drain before anything is
+            # unmapped or freed.
+            torch.cuda.synchronize(self.device)
         self._close_peers()
         cap = ((m + 127) // 128) * 128
         self._bufs = torch.empty(2, cap, self.n, dtype=torch.bfloat16, device=self.device)

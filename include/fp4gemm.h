@@ -119,6 +119,19 @@ int fp4b_device_error(int clear);
  * Asynchronous on `stream`; 0, or -1 bad `which`, -4 launch failure. */
 int fp4b_selftest_bounded_wait(int which, void* stream);
 
+/* Measured tensor-pipe rate of the block-scaled NVFP4 MMA (no counterpart in
+ * the reference): launches one CTA pair per two SMs whose even CTA issues
+ * `stages` x 4 k-blocks of tcgen05.mma.cta_group::2.kind::mxf4nvf4 (M = 256,
+ * K = 64) on operands resident in shared memory -- no loads.  Per k-block: an
+ * MMA of width n0 and, if n1 > 0, a second of width n1 on the same A tile
+ * (n0, n1 multiples of 64 in [64, 256], n0 + n1 <= 384); with sf_copies != 0
+ * also the tcgen05.cp scale copies of the GEMM mainloop (1 atom for A and
+ * sfb_atoms (0..3) for B per k-block).  FLOPs = pairs x stages x 4 x 2 x 256 x
+ * (n0 + n1) x 64, with *pairs_out the pairs launched; the caller times the
+ * launch on `stream` (n0 = 256, n1 = 0, no copies: the dense NVFP4 peak).
+ * Asynchronous; 0, -1 bad arguments (stages in 1..2^20), -4 launch failure. */
+int fp4b_mma_rate(int n0, int n1, int sf_copies, int sfb_atoms, int stages, int* pairs_out, void* stream);
+
 /* Quantize BF16 [rows, cols] (row stride ld elements) into caller buffers:
  * dst_fp4 [rows_pad, k_pad/2], dst_sf rows_pad*k_pad/16 bytes.  Positions
  * outside [rows, cols) quantize as zeros, which reproduces the reference's
@@ -141,7 +154,8 @@ int fp4b_gemm_prequant(const void* a_fp4, const void* a_sf, int m, int m_rows_pa
  * (row stride ldd) with n_out <= the cache's N, optional C (ldc) and bias [n_out].
  * Same values as the reference's pad -> fp4_gemm_run_cached -> unpad -> bias
  * sequence (fp4_gemm.py:324-394), without the pad/unpad copies.  Uses the
- * per-device scratch; asynchronous on `stream`. */
+ * per-device scratch; asynchronous on `stream`.  0 ok; -1 bad arguments or
+ * allocation failure; -2 a geometry the kernels cannot take; -4 launch failure. */
 int fp4b_run_cached_ex(const void* A_bf16, int m, int k_in, int lda, const void* cache_handle, int n_out,
                        const void* C_bf16, int ldc, void* D_bf16, int ldd, const void* bias_bf16, float alpha,
                        float beta, void* stream);
@@ -191,9 +205,11 @@ void* fp4b_weight_cache_import(const void* src_fp4, const void* src_sf, int N, i
  * activations go to a fixed 9 MiB array that is part of the library's device
  * code (16 Mi padded elements: round_up(m,128) * the cache's K must not exceed
  * 16777216, else -1 with a message).  The first call on a device looks up that
- * array's device address, so make it before capturing work into a CUDA graph.
- * All calls on a device share the array: calls that overlap on the GPU race.
- * Arguments, results and return codes as fp4b_run_cached_ex. */
+ * array's device address, so make it before capturing work into a CUDA graph;
+ * if that lookup fails the call returns -1, as an allocation failure does in
+ * fp4b_run_cached_ex.  All calls on a device share the array: calls that
+ * overlap on the GPU race.  Arguments, results and the other return codes as
+ * fp4b_run_cached_ex. */
 int fp4b_run_cached_noalloc(const void* A_bf16, int m, int k_in, int lda, const void* cache_handle, int n_out,
                             const void* C_bf16, int ldc, void* D_bf16, int ldd, const void* bias_bf16, float alpha,
                             float beta, void* stream);
@@ -204,8 +220,10 @@ int fp4b_run_cached_noalloc(const void* A_bf16, int m, int k_in, int lda, const 
  * GPUs' [.., ldd] BF16 outputs mapped with fp4b_ipc_open_handle, each already
  * offset to this rank's first column) with NVLink stores.  The caller orders
  * the ranks after the call (for example with a one-element all-reduce on the
- * same stream).  m > 128, no C, 16-byte aligned output rows.  Asynchronous on
- * `stream`; return codes as fp4b_run_cached_ex. */
+ * same stream).  m > 128, no C.  D and every peer_d[i] must be 16-byte aligned
+ * and ldd a multiple of 8 elements (the epilogue stores 16 bytes at a time);
+ * otherwise -2 before any device work.  Asynchronous on `stream`; other return
+ * codes as fp4b_run_cached_ex. */
 int fp4b_run_cached_peers(const void* A_bf16, int m, int k_in, int lda, const void* cache_handle, int n_out,
                           void* D_bf16, int ldd, void* const* peer_d, int npeers, const void* bias_bf16,
                           void* stream);

@@ -13,9 +13,15 @@
   external library (CUTLASS 3.8, fetched over the network by the reference's
   build.sh) and an SM120 GPU, so it is not built.
 
-Run ``python oracle/build.py`` to build both (the reference step is skipped
-when the reference checkout is absent, e.g. on a GPU box that only uses the
-prebuilt files).
+Where the reference's source is read from: the path in the environment
+variable ``FP4_REFERENCE_LIB_CU`` (the reference's ``fp4_gemm_lib.cu``), else
+``<reference_path>/fp4_gemm_lib.cu`` with ``reference_path`` taken from this
+repository's ``BASELINE.json`` (the build's own record of where the reference
+checkout was surveyed).  When neither exists -- e.g. on a GPU box, which only
+uses the prebuilt files -- the reference step is skipped and a library built
+earlier is kept.
+
+Run ``python oracle/build.py`` to build both.
 """
 from __future__ import annotations
 
@@ -28,10 +34,22 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "libnvfp4_oracle.so")
 REF_DIR = os.path.join(HERE, "_ref")
 REF_SO = os.path.join(REF_DIR, "libref_quant.so")
-# The reference checkout sits beside this repository ("reference/"); FP4_REFERENCE_LIB_CU overrides it.
-REFERENCE_LIB_CU = os.environ.get(
-    "FP4_REFERENCE_LIB_CU",
-    os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference", "fp4_gemm_lib.cu"))
+
+
+def reference_lib_cu() -> str | None:
+    """Location of the reference's fp4_gemm_lib.cu (see the module docstring), or None."""
+    env = os.environ.get("FP4_REFERENCE_LIB_CU")
+    if env:
+        return env
+    baseline = os.path.join(os.path.dirname(HERE), "BASELINE.json")
+    try:
+        import json
+        with open(baseline, encoding="utf-8") as f:
+            root = json.load(f).get("reference_path")
+    except (OSError, ValueError):
+        return None
+    return os.path.join(root, "fp4_gemm_lib.cu") if root else None
+
 
 # Both compiles keep IEEE fp32 semantics: no contraction, no fast-math.
 _FP_FLAGS = ["-O2", "-ffp-contract=off", "-fno-fast-math", "-fopenmp", "-fPIC", "-shared"]
@@ -71,13 +89,14 @@ def extract_reference_quantizer(lib_cu: str) -> str:
 
 def build_ref(force: bool = False) -> str | None:
     """Compile the reference quantizer for the host; None when the reference is absent."""
-    if not os.path.exists(REFERENCE_LIB_CU):
+    lib_cu = reference_lib_cu()
+    if not lib_cu or not os.path.exists(lib_cu):
         return REF_SO if os.path.exists(REF_SO) else None
-    deps = (REFERENCE_LIB_CU, os.path.join(HERE, "ref_shim.h"), os.path.join(HERE, "ref_driver.cpp"))
+    deps = (lib_cu, os.path.join(HERE, "ref_shim.h"), os.path.join(HERE, "ref_driver.cpp"))
     if not force and _newer(REF_SO, *deps):
         return REF_SO
     os.makedirs(REF_DIR, exist_ok=True)
-    section = extract_reference_quantizer(REFERENCE_LIB_CU)
+    section = extract_reference_quantizer(lib_cu)
     with tempfile.TemporaryDirectory() as tmp:
         inc = os.path.join(tmp, "ref_quant_section.inc")
         with open(inc, "w", encoding="utf-8") as f:

@@ -20,10 +20,10 @@
  * Parity is pinned: tests/test_oracle.py checks these functions against the
  * golden vectors in tests/golden/, which tests/golden/make_golden.py produced
  * by running the reference's own quantizer source (compiled for the host by
- * oracle/build_ref.py into oracle/_ref/).
+ * build_ref() in oracle/build.py into oracle/_ref/).
  *
  * Build: gcc -O2 -std=c11 -ffp-contract=off -fno-fast-math -fopenmp -fPIC -shared
- * (oracle/build_oracle.py).  Contraction must stay off so that every product
+ * (build_oracle() in oracle/build.py).  Contraction must stay off so that every product
  * and difference is rounded exactly as the device code rounds it.
  */
 #include <math.h>

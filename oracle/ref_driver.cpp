@@ -1,7 +1,7 @@
 /*
  * ref_driver.cpp -- host driver around the reference's own quantizer source.
  *
- * TEST INFRASTRUCTURE ONLY.  oracle/build_ref.py compiles this file together
+ * TEST INFRASTRUCTURE ONLY.  build_ref() in oracle/build.py compiles this file together
  * with the quantizer section of the reference's fp4_gemm_lib.cu (lines
  * 106-286: the E2M1/UE4M3 codecs, compute_sf_index and
  * quantize_bf16_to_fp4_kernel), which it includes as REF_QUANT_SOURCE.  The

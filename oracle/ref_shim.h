@@ -1,7 +1,7 @@
 /*
  * ref_shim.h -- lets the reference quantizer's CUDA source compile as host C++.
  *
- * TEST INFRASTRUCTURE ONLY (see oracle/build_ref.py).  The reference's
+ * TEST INFRASTRUCTURE ONLY (see oracle/build.py, build_ref).  The reference's
  * quantizer (fp4_gemm_lib.cu:106-286 of VincentKaufmann/fp4-gemm-blackwell)
  * uses only CUDA qualifiers, the bf16->fp32 conversion and libm.  This header
  * maps the qualifiers to host C++, supplies a bit-exact bf16->fp32 conversion

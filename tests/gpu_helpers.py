@@ -53,6 +53,30 @@ def oracle_linear(x: torch.Tensor, w: torch.Tensor, bias=None, alpha=1.0, beta=0
     return out
 
 
+def assert_gemm_close_device(d: torch.Tensor, ref: torch.Tensor, what: str = ""):
+    """assert_gemm_close evaluated where the tensors are (for outputs of
+    hundreds of millions of elements, which are slow to copy to the host)."""
+    assert d.shape == ref.shape, (d.shape, ref.shape)
+    d = d.float()
+    assert bool(torch.isfinite(d).all()), f"{what}: non-finite output"
+    scale = ref.abs().max()
+    err = (d - ref).abs()
+    worst = err.max()
+    assert bool(worst <= REL_TOL * scale + 1e-30), f"{what}: max err {worst.item()} vs scale {scale.item()}"
+    bad = int((err > REL_TOL * ref.abs() + ABS_FRAC * scale).sum())
+    assert bad == 0, f"{what}: {bad} elements out of tolerance, worst {worst.item()}"
+
+
+def fp32_reference_no_tf32(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """a @ b^T in fp32 on the tensors' device with TF32 disabled."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        return a @ b.t()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
 def to_numpy_u8(t: torch.Tensor) -> np.ndarray:
     return t.detach().cpu().numpy().astype(np.uint8, copy=False)
 

@@ -118,3 +118,30 @@ def test_allocation_failures_return_errors():
     assert null_cache and b"cudaMalloc" in msg_q
     assert rc_init == -1 and b"cudaMalloc" in msg_init
     assert rc_pre == -1 and rc_run == -1
+
+
+def test_peer_outputs_must_be_16_byte_aligned(lib):
+    # The column-parallel epilogue stores 16 bytes at a time into D and into
+    # every peer buffer; a misaligned address or row stride is refused with -2
+    # on the host, before the cache handle is even looked up, so no kernel can
+    # fault on it.  (Fake addresses: nothing is dereferenced.)
+    lib.fp4b_last_error.restype = ctypes.c_char_p
+    fn = lib.fp4b_run_cached_peers
+    fn.restype = ctypes.c_int
+    vp = ctypes.c_void_p
+    fn.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int,
+                   ctypes.POINTER(vp), ctypes.c_int, vp, vp]
+
+    def call(d, ldd, peers):
+        arr = (vp * len(peers))(*peers)
+        return fn(0x10000, 256, 512, 512, None, 512, d, ldd, arr, len(peers), None, None)
+
+    assert call(0x20000, 512, [0x30008]) == -2
+    assert b"16-byte aligned" in lib.fp4b_last_error()
+    assert call(0x20000, 512, [0x30000, 0x40004]) == -2   # the second peer is off
+    assert call(0x20008, 512, [0x30000]) == -2            # D itself
+    assert call(0x20000, 508, [0x30000]) == -2            # row stride not a multiple of 8 elements
+    assert call(0x20000, 512, [0x30000, None]) == -2      # NULL peer
+    # aligned everything: the call goes on to the handle check (NULL here) and fails there instead
+    assert call(0x20000, 512, [0x30000, 0x40000]) == -1
+    assert b"cache handle" in lib.fp4b_last_error()

@@ -103,6 +103,9 @@ def _leaving_worker(rank, world, port, q):
         q.put((rank, "returned"))
     except Exception as e:  # the survivor's collective ends with an error instead of waiting for good
         q.put((rank, type(e).__name__))
+    # os._exit skips the queue's feeder thread: flush the message before leaving.
+    q.close()
+    q.join_thread()
     os._exit(0)
 
 
