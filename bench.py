@@ -645,6 +645,8 @@ def run_ours(args):
     for st in sets:
         st["cache"].free()
     if ws > 1:
+        import fp4_gemm_dist as D
+        D.PeerFlagBarrier.close_all()
         dist.barrier()
         dist.destroy_process_group()
     if result is not None:
@@ -670,6 +672,8 @@ def run_stack(args):
                           "ms_per_step": best["ms_per_step"], "higher_is_better": True, "scaling": "strong",
                           "dtype": "nvfp4", "data": "synthetic", "stack": rep}), flush=True)
     if ws > 1:
+        import fp4_gemm_dist as D
+        D.PeerFlagBarrier.close_all()
         dist.barrier()
         dist.destroy_process_group()
 

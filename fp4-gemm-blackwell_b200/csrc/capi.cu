@@ -363,7 +363,7 @@ FP4B_EXPORT int fp4b_run_cached_ex(const void* A, int m, int k_in, int lda, cons
                alpha * c->w_alpha, beta};
     QuantizeArgs q{A, m, k_in, lda, m_pad, c->K, s.a_fp4.ptr, s.a_sf.ptr};
     if (m > 128 && !quantize_check(q) && !gemm_check(g) &&
-        reserve_zeroed(s.sync, (size_t)(1 + (m_pad + 255) / 256) * sizeof(uint32_t))) {
+        reserve_zeroed(s.sync, (size_t)(1 + (m_pad / 128) * ((c->K + 255) / 256)) * sizeof(uint32_t))) {
         // One kernel quantizes the activations and multiplies (CTA-pair path).
         const cudaError_t e = gemm_launch_fused(g, q, reinterpret_cast<uint32_t*>(s.sync.ptr), st);
         if (e != cudaErrorNotSupported) return launch_status(e, "fused quantize+gemm launch");

@@ -54,12 +54,13 @@ int gemm_tile_width(long m, long n, long k_pad, int sms);
 cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream);
 
 // Cached linear with the activation quantization inside the GEMM kernel (the
-// CTA-pair path, M > 128; opt-in with FP4B_FUSE=1): the kernel quantizes `qa` (whose outputs must be
-// g.a_fp4 / g.a_sf) and multiplies.  `sync_words` is a device array of
-// 1 + ceil(m_rows_pad / 256) words that is zero before the first launch; the
-// kernel leaves it zero.  Launches that share `sync_words` must be ordered
-// (same stream).  Returns cudaErrorNotSupported when the fused path does not
-// apply; the caller then runs quantize_launch and gemm_launch.
+// CTA-pair path, M > 128, tiles in one round of CTA pairs; opt-in with
+// FP4B_FUSE=1): the kernel quantizes `qa` (whose outputs must be g.a_fp4 /
+// g.a_sf) and multiplies.  `sync_words` is a device array of
+// 1 + (m_rows_pad / 128) * ceil(k_pad / 256) words that is zero before the
+// first launch; the kernel leaves it zero.  Launches that share `sync_words`
+// must be ordered (same stream).  Returns cudaErrorNotSupported when the fused
+// path does not apply; the caller then runs quantize_launch and gemm_launch.
 // GEMM whose output tile is also stored into `npeers` (1..7) other BF16
 // buffers with the same row stride (other GPUs' memory mapped into this
 // process, each offset to the columns this rank computes): the column-parallel

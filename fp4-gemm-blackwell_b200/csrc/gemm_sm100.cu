@@ -119,12 +119,21 @@ struct Params {
     // the BF16 activations described by `q` into a_fp4 / a_sf itself.
     qcore::QuantParams q;
     const qcore::QuantTables* qtab;
-    uint32_t* ready;  // [m_tiles] finished shares per 256-row tile, then one CTA-exit counter
+    // [a_tiles128][a_stages] units done per 128-row tile of A and K-stage, then
+    // one CTA-exit counter (ready_count = a_tiles128 * a_stages words before it).
+    uint32_t* ready;
+    int a_groups, a_stages, ready_count;  // 64-row groups of the padded A, K-stages
     // Column-parallel output (pair kernel, TMA-store epilogue): every tile is
     // also written to npeers other [m, ldd] BF16 buffers (other GPUs' memory
-    // mapped into this process), each already offset to this rank's columns.
-    __nv_bfloat16* peer_d[kMaxPeers];
+    // mapped into this process), each already offset to this rank's columns;
+    // their tensor maps are the kernel's PeerMaps argument.
     int npeers;
+};
+
+// Output tensor maps of the peer buffers (column-parallel mode); all zero and
+// unused otherwise.
+struct PeerMaps {
+    CUtensorMap map[kMaxPeers];
 };
 
 // Tile t -> (row tile, column tile) in groups of kTileGroupRows rows of A: the
@@ -271,12 +280,15 @@ __device__ __forceinline__ void convert_chunk(const Params& p, const uint32_t (&
 }
 
 // Writes a converted chunk into the warp's 64B-swizzled staging buffer and
-// stores it with one TMA store (issued by a rotating lane), plus the copies to
-// peer GPUs.
-__device__ __forceinline__ void store_staged_chunk(const Params& p, const CUtensorMap* tmap_d,
+// stores it with one TMA store (issued by a rotating lane), plus one TMA store
+// of the same staged chunk into each peer GPU's buffer (stores over NVLink; no
+// multicast, no load from another GPU).
+// `fresh`: the buffer has not been used since the operand ring went idle, so
+// no earlier store can still be reading it.
+__device__ __forceinline__ void store_staged_chunk(const Params& p, const CUtensorMap* tmap_d, const PeerMaps* pm,
                                                    const uint32_t (&packed)[16], uint8_t* buf, int row0, int n,
-                                                   int lane, int chunk_iter) {
-    if (lane == ((chunk_iter - 1) & 31)) ptx::bulk_wait_group_read<0>();
+                                                   int lane, int chunk_iter, bool fresh = false) {
+    if (!fresh && lane == ((chunk_iter - 1) & 31)) ptx::bulk_wait_group_read<0>();
     __syncwarp();
     uint8_t* row = buf + 64 * lane;
     const int sw = (lane >> 1) & 3;
@@ -288,27 +300,8 @@ __device__ __forceinline__ void store_staged_chunk(const Params& p, const CUtens
     __syncwarp();
     if (lane == (chunk_iter & 31)) {
         ptx::tma_store_2d(tmap_d, buf, n, row0);
+        for (int d = 0; d < p.npeers; ++d) ptx::tma_store_2d(&pm->map[d], buf, n, row0);
         ptx::bulk_commit_group();
-    }
-    if (p.npeers > 0) {
-        // Peer copies over NVLink with plain 16-byte stores: the staged chunk is
-        // read back row by row, four lanes per 64-byte row segment.
-#pragma unroll
-        for (int pass = 0; pass < 4; ++pass) {
-            const int rr = pass * 8 + (lane >> 2), u = lane & 3;
-            const uint4 v = *reinterpret_cast<const uint4*>(buf + 64 * rr + 16 * (u ^ ((rr >> 1) & 3)));
-            const int grow = row0 + rr, gcol = n + 8 * u;
-            if (grow >= p.m || gcol >= p.n_out) continue;
-            const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&v);
-            for (int d = 0; d < p.npeers; ++d) {
-                __nv_bfloat16* dst = p.peer_d[d] + (size_t)grow * p.ldd + gcol;
-                if (gcol + 8 <= p.n_out) {
-                    *reinterpret_cast<uint4*>(dst) = v;
-                } else {
-                    for (int i = 0; i < 8 && gcol + i < p.n_out; ++i) dst[i] = vb[i];
-                }
-            }
-        }
     }
 }
 
@@ -487,6 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint64_t sfb_s = sfbdesc0 + (uint64_t)((s * C::SFB_BYTES) >> 4);
                 const uint32_t first = (ks == 0) ? 0u : 1u;
                 if (ptx::elect_one()) {
+                    // Each k-block's scale copies right before its MMA (see the pair kernel).
 #pragma unroll
                     for (int j = 0; j < kKbPerStage; ++j) {
                         if (j < nkb) {
@@ -497,11 +491,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     ptx::tc_cp_32x128b_warpx4(
                                         sfb_t + j * 4 * C::NRT + 4 * r,
                                         sfb_s + (uint64_t)(((r * kKbPerStage + j) * kAtomBytes) >> 4));
-                        }
-                    }
-#pragma unroll
-                    for (int j = 0; j < kKbPerStage; ++j) {
-                        if (j < nkb) {
                             const uint32_t koff = (uint32_t)(((j >> 2) * C::A_CHUNK + 32 * (j & 3)) >> 4);
                             const uint32_t kofb = (uint32_t)(((j >> 2) * C::B_CHUNK + 32 * (j & 3)) >> 4);
                             ptx::tc_mma_nvf4(acc, a_s + koff, b_s + kofb, idesc, sfa_t + 4 * j,
@@ -640,94 +629,130 @@ struct PairCfg {
     static constexpr uint32_t TMEM_SFB = TMEM_SFA + 4 * kKbPerStage;
     static_assert(B_SUB_BYTES % 1024 == 0 && B_SUB1_BYTES % 1024 == 0, "B stage must keep the 128B-swizzle alignment");
     static_assert(STAGE_BYTES % 1024 == 0, "epilogue buffers must stay 1024-byte aligned");
+    static_assert(STAGES * STAGE_BYTES >= 4 * (TW / 32) * 2048, "the idle ring stages every chunk of the last tile");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
     static_assert(TMEM_SFA + SF_COLS <= kTmemCols, "TMEM budget exceeded");
 };
 
 constexpr uint64_t kAbortDrainNs = 200000;  // after an abort, let issued copies land
 constexpr int kPairThreads = 416;
+constexpr int kPairThreadsFused = 448;  // + the publisher warp
 constexpr int kPairMmaWarp = 8;
 constexpr int kPairFirstProducer = 9;
 
-// Fused mode: the epilogue warps of every CTA quantize an equal share of each
-// 256-row tile of A, tile by tile.  A warp takes every kWarps-th 32-block chunk
-// of its CTA's share, four chunks (one block per lane each) per group, and
-// issues the loads of its next group (of the same or a later tile) before
-// quantizing the current one.  Once a warp is past its last chunk of a tile
-// it adds one to ready[tile]; the A producers of that tile wait for
-// gridDim.x * kWarps.  The counters start at zero (the last CTA to exit
-// resets them).
-struct QuantGroup {
-    uint32_t w[4][8], r[4], kb[4], idx[4], end[4];
-};
+// Fused mode (FUSED): the kernel quantizes its BF16 activations itself, for
+// problems whose tiles fit in one round of CTA pairs, so that the epilogue
+// warps are idle while the MMAs run.  The padded rows of A are cut into units
+// of 64 rows x one 256-wide K-stage (16 blocks of 16), ordered K-stage by
+// K-stage: unit u covers K-stage u / R of the 64-row group u % R (R = rows_pad
+// / 64).  CTA c of the grid quantizes units c, c + G, c + 2G, ... with its
+// eight epilogue warps: warp w takes rows [8w, 8w + 8) of the unit and lane l
+// the block kb = 16 ks + (l & 15) of rows 2j + (l >> 4), j = 0..3, so each
+// half warp reads 512 contiguous bytes of one row, and four consecutive lanes
+// hold four consecutive blocks of a row (one 4-byte scale store).  The loads
+// of the CTA's next unit are in flight while the current unit is quantized.
+// Once a unit's codes and scales are stored, the eight warps and a publisher
+// warp meet at a named barrier; the publisher, which has no loads of its own
+// in flight (a fence would wait for them), fences and adds one to the counter
+// of the unit's 128-row tile and K-stage.  The A and scale-A producers of a
+// stage wait (bounded) until their tile's counter for that stage reaches 2.
+// The last CTA to exit zeroes the counters for the next launch.
+constexpr int kUnitRows = 64;
+constexpr int kUnitBlocks = 4;           // blocks per lane per unit
+constexpr uint32_t kUnitBarrier = 2;      // named barrier id (1 is the epilogue warps' own)
+constexpr int kPairPublisherWarp = 13;   // fused kernel only
 
-// Loads this warp's next group at or after chunk cursor (j, c); c = ~0 means
-// "first chunk of tile j".  Returns false when the warp has no chunks left;
-// on success j is the group's tile.
+__device__ __forceinline__ void load_block_rk(const qcore::QuantParams& q, uint32_t r, uint32_t kb,
+                                              uint32_t (&w)[8]) {
+    const uint32_t c0 = kb * kSfVec;
+    if (kb >= q.nsb) {  // past the padded K of a half-width last K-stage: not stored
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[i] = 0u;
+    } else if (q.vec_ok && r < q.rows && c0 + kSfVec <= q.cols) {
+        const uint4* g = reinterpret_cast<const uint4*>(q.src + (size_t)r * q.ld + c0);
+        const uint4 v0 = __ldcs(g);
+        const uint4 v1 = __ldcs(g + 1);
+        w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
+        w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
+    } else {
+        // Ragged edge, padding rows or columns, unaligned rows: element loads, zeros outside.
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[i] = qcore::load_pair(q.src, q.ld, q.rows, q.cols, r, c0 + 2 * i);
+    }
+}
+
+// Row and block of this lane's j-th block of unit u.
+__device__ __forceinline__ void unit_block(uint32_t u, uint32_t R, int warp, int lane, int j, uint32_t& r,
+                                           uint32_t& kb) {
+    const uint32_t ks = u / R, grp = u - ks * R;
+    r = grp * kUnitRows + 8u * (uint32_t)warp + 2u * (uint32_t)j + ((uint32_t)lane >> 4);
+    kb = ks * 16u + ((uint32_t)lane & 15u);
+}
+
+__device__ __forceinline__ void load_unit(const qcore::QuantParams& q, uint32_t u, uint32_t R, int warp, int lane,
+                                          uint32_t (&w)[kUnitBlocks][8]) {
+#pragma unroll
+    for (int j = 0; j < kUnitBlocks; ++j) {
+        uint32_t r, kb;
+        unit_block(u, R, warp, lane, j, r, kb);
+        load_block_rk(q, r, kb, w[j]);
+    }
+}
+
+__device__ __forceinline__ void store_unit(const qcore::QuantParams& q, uint32_t u, uint32_t R, int warp, int lane,
+                                           const uint32_t (&w)[kUnitBlocks][8], const qcore::SmemTables& tab) {
+#pragma unroll
+    for (int j = 0; j < kUnitBlocks; ++j) {
+        uint32_t r, kb;
+        unit_block(u, R, warp, lane, j, r, kb);
+        qcore::quantize_and_store(q, r * q.nsb + kb, kb < q.nsb ? q.total : 0u, w[j], r, kb, (uint32_t)lane, tab);
+    }
+}
+
+// The eight quantizing warps: every unit of this CTA, one named barrier per
+// unit (the publisher takes the same number).
 template <int kWarps>
-__device__ __forceinline__ bool load_next_group(const Params& p, int warp, int lane, int& j, uint32_t& c,
-                                                QuantGroup& g) {
+__device__ __forceinline__ void quantize_units(const Params& p, const qcore::SmemTables& tab, int warp, int lane) {
     const qcore::QuantParams& q = p.q;
-    const uint32_t G = gridDim.x, per_tile = 256u * q.nsb;
-    for (; j < p.m_tiles; ++j, c = 0xFFFFFFFFu) {
-        const uint32_t b0 = (uint32_t)j * per_tile;
-        const uint32_t b1 = min(b0 + per_tile, q.total);
-        const uint32_t nch = (b1 - b0) >> 5;
-        const uint32_t c1 = (uint32_t)(((uint64_t)nch * (blockIdx.x + 1)) / G);
-        if (c == 0xFFFFFFFFu) c = (uint32_t)(((uint64_t)nch * blockIdx.x) / G) + (uint32_t)warp;
-        if (c < c1) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t ci = c + (uint32_t)(i * kWarps);
-                g.idx[i] = b0 + ci * 32u + (uint32_t)lane;
-                g.end[i] = ci < c1 ? b1 : 0u;
-                qcore::load_block(q, g.idx[i], g.end[i], g.w[i], g.r[i], g.kb[i]);
-            }
-            c += 4u * kWarps;
-            return true;
-        }
+    const uint32_t R = (uint32_t)p.a_groups, U = R * (uint32_t)p.a_stages, G = gridDim.x;
+    uint32_t u = blockIdx.x;
+    if (u >= U) return;
+    uint32_t wa[kUnitBlocks][8], wb[kUnitBlocks][8];
+    load_unit(q, u, R, warp, lane, wa);
+    for (;;) {
+        // Two register sets used in turn: the next unit's loads are in flight
+        // while the current one is quantized.
+        const uint32_t u1 = u + G;
+        if (u1 < U) load_unit(q, u1, R, warp, lane, wb);
+        store_unit(q, u, R, warp, lane, wa, tab);
+        __syncwarp();
+        ptx::named_barrier(kUnitBarrier, (kWarps + 1) * 32);
+        if (u1 >= U) break;
+        const uint32_t u2 = u1 + G;
+        if (u2 < U) load_unit(q, u2, R, warp, lane, wa);
+        store_unit(q, u1, R, warp, lane, wb, tab);
+        __syncwarp();
+        ptx::named_barrier(kUnitBarrier, (kWarps + 1) * 32);
+        if (u2 >= U) break;
+        u = u2;
     }
-    return false;
 }
 
-// Count tiles [counted, upto) as finished by this warp.
-__device__ __forceinline__ void count_tiles(const Params& p, int lane, int& counted, int upto) {
-    if (counted >= upto) return;
-    __syncwarp();  // every lane's stores of those tiles are issued
-    if (lane == 0) {
-        ptx::fence_proxy_async_global();
-        __threadfence();
-        for (int t = counted; t < upto; ++t) atomicAdd(p.ready + t, 1u);
-    }
-    counted = upto;
-}
-
+// The publisher warp: after each unit's barrier, make the unit's stores
+// visible to every CTA's TMA loads and count the unit.
 template <int kWarps>
-__device__ __forceinline__ void quantize_phase(const Params& p, const qcore::SmemTables& tab, int warp, int lane) {
-    int j = 0, counted = 0;
-    uint32_t c = 0xFFFFFFFFu;
-    QuantGroup cur, nxt;
-    bool have = load_next_group<kWarps>(p, warp, lane, j, c, cur);
-    int cur_tile = have ? j : p.m_tiles;
-    count_tiles(p, lane, counted, cur_tile);  // tiles before the first group hold nothing of this warp
-    while (have) {
-        int j2 = j;
-        uint32_t c2 = c;
-        const bool have2 = load_next_group<kWarps>(p, warp, lane, j2, c2, nxt);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            qcore::quantize_and_store(p.q, cur.idx[i], cur.end[i], cur.w[i], cur.r[i], cur.kb[i], (uint32_t)lane, tab);
-        const int next_tile = have2 ? j2 : p.m_tiles;
-        count_tiles(p, lane, counted, next_tile);  // tiles before the next group are done
-        have = have2;
-        if (have) {
-            cur = nxt;
-            cur_tile = j2;
-            j = j2;
-            c = c2;
+__device__ __forceinline__ void publish_units(const Params& p, int lane) {
+    const uint32_t R = (uint32_t)p.a_groups, U = R * (uint32_t)p.a_stages;
+    for (uint32_t u = blockIdx.x; u < U; u += gridDim.x) {
+        ptx::named_barrier(kUnitBarrier, (kWarps + 1) * 32);
+        if (lane == 0) {
+            const uint32_t ks = u / R, grp = u - ks * R;
+            ptx::fence_proxy_async_global();
+            __threadfence();
+            atomicAdd(p.ready + (grp >> 1) * (uint32_t)p.a_stages + ks, 1u);
         }
+        __syncwarp();
     }
-    count_tiles(p, lane, counted, p.m_tiles);
 }
 
 // Epilogue of a CTA pair's last tile by a team of warps per TMEM lane
@@ -735,11 +760,15 @@ __device__ __forceinline__ void quantize_phase(const Params& p, const qcore::Sme
 // whose roles have ended (8 and 12 on quadrant 0, 9, 10, 11 on quadrants 1-3).
 // Member ti of ts takes 32-column chunks c = ti, ti + ts, ...
 // Chunk c's BF16 bias was staged by epilogue warp q + 4 (c & 1) at uint4
-// offset 4 (c >> 1).  tq: TMEM address of the quadrant's accumulator; buf: the
-// member's 2 KB staging buffer; m: this lane's output row.
+// offset 4 (c >> 1).  tq: TMEM address of the quadrant's accumulator; ring:
+// the operand ring, idle once the last tile's MMAs have completed, in which
+// chunk c of quadrant q is staged in a 2 KB slot of its own (q * CH + c), so no
+// chunk waits for an earlier TMA store to finish reading its buffer; m: this
+// lane's output row.
 template <int TW>
-__device__ __forceinline__ void team_epilogue(const Params& p, const CUtensorMap* tmap_d, uint32_t tq,
-                                              const uint4* sBias, int q, int ti, int ts, uint8_t* buf,
+__device__ __forceinline__ void team_epilogue(const Params& p, const CUtensorMap* tmap_d, const PeerMaps* pm,
+                                              uint32_t tq,
+                                              const uint4* sBias, int q, int ti, int ts, uint8_t* ring,
                                               int& chunk_iter, int m, int n0, int lane) {
     constexpr int CH = TW / 32;
 #pragma unroll 1
@@ -752,7 +781,8 @@ __device__ __forceinline__ void team_epilogue(const Params& p, const CUtensorMap
             uint32_t pk[16];
             convert_chunk(p, r, sBias + (q + 4 * (c & 1)) * (TW / 16) + 4 * (c >> 1), pk);
             if (m - lane < p.m)  // the warp's 32 rows start inside D
-                store_staged_chunk(p, tmap_d, pk, buf, m - lane, n0 + 32 * c, lane, chunk_iter++);
+                store_staged_chunk(p, tmap_d, pm, pk, ring + (size_t)(q * CH + c) * 2048, m - lane, n0 + 32 * c,
+                                   lane, chunk_iter++, true);
         } else if (m < p.m) {
             store_chunk(p, r, m, n0 + 32 * c);
         }
@@ -760,11 +790,12 @@ __device__ __forceinline__ void team_epilogue(const Params& p, const CUtensorMap
 }
 
 template <int BN, int STAGES, bool FUSED, int NSUB, int BN1>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FUSED ? kPairThreadsFused : kPairThreads, 1)
     nvf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_b1,
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-                          const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ Params p) {
+                          const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ Params p,
+                          const __grid_constant__ PeerMaps pm) {
     using C = PairCfg<BN, STAGES, NSUB, BN1>;
     constexpr int TW = C::TW;
     constexpr int TILE_M = 2 * kBM;
@@ -837,12 +868,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     // writes global memory.
     ptx::launch_dependents();
 
-    if (warp >= kPairFirstProducer) {
+    if (FUSED && warp == kPairPublisherWarp) {
+        // ------------------------------------------------------------ publisher (fused mode)
+        publish_units<kPairEpiWarps>(p, lane);
+    } else if (warp >= kPairFirstProducer) {
         // ------------------------------------------------------------ producers (both CTAs)
         const int role = warp - kPairFirstProducer;  // 0 A, 1 B, 2 scale-A, 3 scale-B
         const uint32_t full0 = ptx::map_to_cta(ptx::smem_u32(full), 0);
         int it = 0;
-        int ready_tile = -1;  // fused mode: last 256-row tile of A known to be quantized
         bool stop = false;
         for (int t = pair; t < p.num_tiles && !stop; t += npairs) {
             int m_tile, n_tile;
@@ -870,10 +903,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     break;
                 }
                 if constexpr (FUSED) {
-                    if ((role == 0 || role == 2) && m_tile != ready_tile) {
-                        // Every CTA's share of this tile of A is quantized and visible to TMA.
+                    // A CTA whose 128 rows lie wholly past the padded rows of A (the
+                    // second half of a last 256-row tile when rows_pad % 256 == 128)
+                    // has no units to wait for: its TMA boxes read zeros.
+                    if ((role == 0 || role == 2) && 2 * m_tile + (int)rank < (p.a_groups >> 1)) {
+                        // Both 64-row units of this CTA's 128 rows of A for this K-stage
+                        // are quantized and visible to TMA.
                         bool ok = true;
-                        if (lane == 0) ok = ptx::wait_counter_geq(p.ready + m_tile, gridDim.x * kPairEpiWarps);
+                        if (lane == 0)
+                            ok = ptx::wait_counter_geq(p.ready + (size_t)(2 * m_tile + (int)rank) * p.a_stages + ks,
+                                                       2u);
                         ok = __shfl_sync(0xffffffffu, ok, 0);
                         if (!ok) {
                             if (lane == 0) {
@@ -884,7 +923,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                             break;
                         }
                         ptx::fence_proxy_async_global();
-                        ready_tile = m_tile;
                     }
                 }
                 // The B copies of the NSUB MMAs go out from different lanes.
@@ -962,6 +1000,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     const uint64_t sfb_s = sfbdesc0 + (uint64_t)((s * C::SFB_BYTES) >> 4);
                     const uint32_t first = (ks == 0) ? 0u : 1u;
                     if (ptx::elect_one()) {
+                        // Each k-block's scale copies go right before its own MMAs:
+                        // on B200 the tensor pipe then overlaps them with the previous
+                        // k-block's MMAs (issuing a stage's copies first cost ~5 % of
+                        // the MMA rate of the 320-wide tile, ~7 % of the 384-wide one).
 #pragma unroll
                         for (int j = 0; j < kKbPerStage; ++j) {
                             if (j < nkb) {
@@ -972,11 +1014,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                                     ptx::tc_cp_32x128b_warpx4_pair(
                                         sfb_t + j * 4 * C::NRT + 4 * r,
                                         sfb_s + (uint64_t)(((r * kKbPerStage + j) * kAtomBytes) >> 4));
-                            }
-                        }
-#pragma unroll
-                        for (int j = 0; j < kKbPerStage; ++j) {
-                            if (j < nkb) {
                                 const uint32_t koff = (uint32_t)((32 * j) >> 4);
 #pragma unroll
                                 for (int u = 0; u < NSUB; ++u)
@@ -1012,7 +1049,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             static_assert(C::EPI_BYTES >= qcore::kSmemTableBytes, "tables must fit the staging buffers");
             const qcore::SmemTables tab = qcore::copy_tables(p.qtab, sEpi, threadIdx.x, kPairEpiWarps * 32);
             ptx::named_barrier(1, kPairEpiWarps * 32);
-            quantize_phase<kPairEpiWarps>(p, tab, warp, lane);
+            quantize_units<kPairEpiWarps>(p, tab, warp, lane);
             ptx::named_barrier(1, kPairEpiWarps * 32);  // tables no longer read: buffers free
         }
         int chunk_iter = 0;
@@ -1049,8 +1086,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     }
                     break;
                 }
-                team_epilogue<TW>(p, &tmap_d, tmem + ((uint32_t)(q * 32) << 16) + b * TW, sBias, q, h,
-                                  q == 0 ? 4 : 3, epi, chunk_iter, m, n0, lane);
+                team_epilogue<TW>(p, &tmap_d, &pm, tmem + ((uint32_t)(q * 32) << 16) + b * TW, sBias, q, h,
+                                  q == 0 ? 4 : 3, smem, chunk_iter, m, n0, lane);
                 continue;
             }
             // Only a later tile of this pair that reuses accumulator b waits for it.
@@ -1082,8 +1119,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                         if (lane == 0) ptx::mbar_arrive_cluster(acc_empty0 + (uint32_t)b * 8u);
                     }
                     if (m - lane < p.m) {  // the warp's 32 rows start inside D
-                        if (in0) store_staged_chunk(p, &tmap_d, pa, epi, m - lane, n0 + 32 * c0, lane, chunk_iter++);
-                        if (in1) store_staged_chunk(p, &tmap_d, pb, epi, m - lane, n0 + 32 * c1, lane, chunk_iter++);
+                        if (in0)
+                            store_staged_chunk(p, &tmap_d, &pm, pa, epi, m - lane, n0 + 32 * c0, lane, chunk_iter++);
+                        if (in1)
+                            store_staged_chunk(p, &tmap_d, &pm, pb, epi, m - lane, n0 + 32 * c1, lane, chunk_iter++);
                     }
                 } else {
                     if (m < p.m) {
@@ -1102,10 +1141,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             }
         }
         ptx::bulk_wait_group_all();  // every lane's stores have read shared memory and written D
-        if (p.npeers > 0) __threadfence_system();  // peer stores visible before the kernel ends
+        if (p.npeers > 0) {
+            // The peer stores (async proxy) are complete; order them before the
+            // rank-ordering signal that follows the kernel.
+            ptx::fence_proxy_async_global();
+            __threadfence_system();
+        }
     }
 
-    if (warp >= kPairMmaWarp && !__any_sync(0xffffffffu, aborted(s_abort))) {
+    if (warp >= kPairMmaWarp && warp < kPairPublisherWarp && !__any_sync(0xffffffffu, aborted(s_abort))) {
         // -------------------------------------------- MMA and producer warps: help with the last tile
         const int q = warp & 3;
         const int ti = warp == kPairThreads / 32 - 1 ? 3 : 2;  // warp 12 is quadrant 0's fourth member
@@ -1128,10 +1172,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             ptx::tc_fence_after();
             // Every MMA has completed and no load is left: the operand ring is idle.
             int chunk_iter = 0;
-            team_epilogue<TW>(p, &tmap_d, tmem + ((uint32_t)(q * 32) << 16) + b * TW, sBias, q, ti, q == 0 ? 4 : 3,
-                              smem + (warp - kPairMmaWarp) * 2048, chunk_iter, m, n0, lane);
+            team_epilogue<TW>(p, &tmap_d, &pm, tmem + ((uint32_t)(q * 32) << 16) + b * TW, sBias, q, ti,
+                              q == 0 ? 4 : 3, smem, chunk_iter, m, n0, lane);
             ptx::bulk_wait_group_all();
-            if (p.npeers > 0) __threadfence_system();
+            if (p.npeers > 0) {
+                ptx::fence_proxy_async_global();
+                __threadfence_system();
+            }
         }
     }
 
@@ -1149,12 +1196,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     }
     if constexpr (FUSED) {
         // The last CTA to get here (all producers are past their waits) zeroes
-        // the tile counters for the next launch.
+        // the unit counters for the next launch.
         if (threadIdx.x == 0) {
             __threadfence();
-            if (atomicAdd(p.ready + p.m_tiles, 1u) == gridDim.x - 1) {
-                for (int j = 0; j < p.m_tiles; ++j) atomicExch(p.ready + j, 0u);
-                atomicExch(p.ready + p.m_tiles, 0u);
+            if (atomicAdd(p.ready + p.ready_count, 1u) == gridDim.x - 1) {
+                for (int j = 0; j < p.ready_count; ++j) atomicExch(p.ready + j, 0u);
+                atomicExch(p.ready + p.ready_count, 0u);
                 __threadfence();
             }
         }
@@ -1276,7 +1323,7 @@ Params make_params(const GemmArgs& g, int bn, int tile_m) {
 
 // Clusters of two resident at once for a pair kernel (one CTA per SM).
 template <typename K>
-int max_pairs(K kernel, int smem, int sms) {
+int max_pairs(K kernel, int smem, int sms, int threads) {
     static int cached[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1284,7 +1331,7 @@ int max_pairs(K kernel, int smem, int sms) {
     if (c == 0) {
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
-        cfg.blockDim = dim3(kPairThreads, 1, 1);
+        cfg.blockDim = dim3(threads, 1, 1);
         cfg.dynamicSmemBytes = smem;
         int n = 0;
         if (cudaOccupancyMaxActiveClusters(&n, (const void*)kernel, &cfg) != cudaSuccess || n <= 0) {
@@ -1320,21 +1367,30 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const Q
     const bool no_c = !g.c || g.beta == 0.0f;
     const bool d_ok = (reinterpret_cast<uintptr_t>(g.d) & 15) == 0 && g.ldd % 8 == 0;
     if (no_c && d_ok && make_output_map(&md, g.d, g.m, g.n_out, g.ldd)) p.tma_store = 1;
+    PeerMaps pm;
+    memset(&pm, 0, sizeof(pm));
     if (npeers > 0) {
         if (!p.tma_store || npeers > kMaxPeers) return cudaErrorNotSupported;
-        for (int i = 0; i < npeers; ++i) p.peer_d[i] = static_cast<__nv_bfloat16*>(peers[i]);
+        for (int i = 0; i < npeers; ++i)
+            if (!make_output_map(&pm.map[i], peers[i], g.m, g.n_out, g.ldd)) return cudaErrorNotSupported;
         p.npeers = npeers;
     }
+    constexpr int threads = FUSED ? kPairThreadsFused : kPairThreads;
+    const int pairs = max_pairs(kernel, C::SMEM_BYTES, sms, threads);
     if constexpr (FUSED) {
         p.qtab = quant_tables_device();
         if (!p.qtab || !qa || !sync_words) return cudaErrorInvalidValue;
+        // One round of tiles only: the epilogue warps quantize before their first epilogue.
+        if (p.num_tiles > pairs) return cudaErrorNotSupported;
         p.q = make_quant_params(*qa);
         p.ready = sync_words;
+        p.a_groups = (int)(g.m_rows_pad / kUnitRows);
+        p.a_stages = (int)((g.k_pad + 255) / 256);
+        p.ready_count = (int)(g.m_rows_pad / 128) * p.a_stages;
     }
-    const int pairs = max_pairs(kernel, C::SMEM_BYTES, sms);
     const int grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);
-    return launch_dependent(kernel, dim3(grid), dim3(kPairThreads), C::SMEM_BYTES, stream, ma, mb, mb1, msa, msb, md,
-                            p);
+    return launch_dependent(kernel, dim3(grid), dim3(threads), C::SMEM_BYTES, stream, ma, mb, mb1, msa, msb, md, p,
+                            pm);
 }
 
 template <int BN, int STAGES, int CHUNKS>
@@ -1415,9 +1471,8 @@ int choose_bn_pair(long m, long n, long k_pad, int sms) {
 
 cudaError_t gemm_launch_fused(const GemmArgs& g, const QuantizeArgs& qa, uint32_t* sync_words,
                               cudaStream_t stream) {
-    // Opt-in (FP4B_FUSE=1): with 8 quantizing warps per SM the quantize phase is
-    // latency-bound and delays the first tiles; on B200 the headline step took
-    // 60 us fused against 43 us for the quantize kernel followed by the GEMM.
+    // Opt-in for now (FP4B_FUSE=1); problems whose tiles need more than one
+    // round of CTA pairs return cudaErrorNotSupported (two kernels instead).
     const char* env = getenv("FP4B_FUSE");
     if (!env || atoi(env) == 0 || g.m <= kBM || (getenv("FP4B_PAIR") && atoi(getenv("FP4B_PAIR")) == 0))
         return cudaErrorNotSupported;
@@ -1432,8 +1487,8 @@ cudaError_t gemm_launch_fused(const GemmArgs& g, const QuantizeArgs& qa, uint32_
         case 256: return launch_pair<256, 5, true>(g, stream, sms, &qa, sync_words);
         case 192: return launch_pair<192, 6, true>(g, stream, sms, &qa, sync_words);
         case 128: return launch_pair<128, 7, true>(g, stream, sms, &qa, sync_words);
-        case 384:  // no fused two-MMA tiles
-        case 320: return launch_pair<192, 6, true>(g, stream, sms, &qa, sync_words);
+        case 384: return launch_pair<192, 4, true, 2>(g, stream, sms, &qa, sync_words);
+        case 320: return launch_pair<128, 4, true, 2, 192>(g, stream, sms, &qa, sync_words);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -82,6 +82,7 @@ _bind("fp4b_ipc_get_handle", _i, [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_
 _bind("fp4b_ipc_open_handle", _vp, [ctypes.c_char_p, ctypes.c_long])
 _bind("fp4b_ipc_close", _i, [_vp, ctypes.c_long])
 _bind("fp4b_mma_rate", _i, [_i, _i, _i, _i, _i, ctypes.POINTER(_i), _vp])
+_bind("fp4b_peer_barrier", _i, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_i), _i, _i, ctypes.c_ulonglong, _vp])
 
 # Query scale factor vector size
 SF_VEC_SIZE = _lib.fp4_gemm_sf_vec_size()
@@ -659,6 +660,19 @@ def ipc_open(handle: bytes, offset: int, device) -> int:
 def ipc_close(ptr: int, offset: int, device):
     with torch.cuda.device(device):
         _lib.fp4b_ipc_close(ptr, offset)
+
+
+def peer_barrier(my_flags: torch.Tensor, peer_flag_ptrs, peer_ranks, my_rank: int, epoch: int) -> None:
+    """Queue fp4b_peer_barrier on the current stream of my_flags' device: signal
+    `epoch` to every peer (their flag arrays, mapped at peer_flag_ptrs) and wait
+    until every peer in peer_ranks has signalled it to this rank."""
+    n = len(peer_flag_ptrs)
+    ptrs = (_vp * n)(*peer_flag_ptrs)
+    ranks = (_i * n)(*peer_ranks)
+    with torch.cuda.device(my_flags.device):
+        rc = _lib.fp4b_peer_barrier(my_flags.data_ptr(), ptrs, ranks, n, my_rank, epoch, _stream_ptr(my_flags.device))
+    if rc != 0:
+        raise RuntimeError(f"fp4b_peer_barrier failed with error code {rc} ({_last_error()})")
 
 
 def run_cached_peers(x: torch.Tensor, cache: "FP4WeightCache", out: torch.Tensor, peer_ptrs) -> None:

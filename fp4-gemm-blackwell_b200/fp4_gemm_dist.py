@@ -14,8 +14,10 @@ single-GPU kernels of ``fp4_gemm``:
   as [M, N] on every rank, in one of two ways:
     - "p2p": the GEMM epilogue itself stores every output tile into the [M, N]
       buffers of all ranks (CUDA IPC mappings of the peers' buffers, NVLink
-      stores), then a one-element all-reduce on the stream orders the ranks.
-      No gather buffer, no re-layout, the transfer overlaps the tiles.
+      stores), then a flag barrier on the GPU (``PeerFlagBarrier``: one warp
+      signals every peer and waits for every peer's signal) orders the ranks.
+      No gather buffer, no re-layout, no collective; the transfer overlaps the
+      tiles.
     - "nccl": one NCCL all-gather of equal-size, zero-padded slices and a
       re-layout.  Used when "p2p" does not apply (M <= 128, N not a multiple
       of 8, a single rank) or when asked for.
@@ -109,6 +111,67 @@ class DataParallelFP4Linear:
         self.cache.free()
 
 
+class PeerFlagBarrier:
+    """The column-parallel ranks' ordering step without a collective.
+
+    Every rank owns a zeroed array of 8 uint64 flag slots, mapped by every
+    other rank with CUDA IPC.  ``wait()`` queues fp4b_peer_barrier on the
+    current stream: it stores the next epoch into this rank's slot of every
+    peer's array and waits (on the GPU, bounded) until every peer has stored
+    that epoch into this rank's array.  Every rank of the group must call
+    ``wait()`` the same number of times, in the same order (the epochs then
+    agree).  One barrier serves all the linears of a group (``for_group``).
+    If a peer does not arrive within 10 s the wait gives up and records code
+    10 in the device error word (``fp4_gemm.device_error()``)."""
+
+    _by_group: dict = {}
+
+    def __init__(self, group, device):
+        import fp4_gemm
+        self.group = group
+        self.device = device
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.flags = torch.zeros(8, dtype=torch.int64, device=device)
+        mine = fp4_gemm.ipc_handle(self.flags)
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=group)
+        self.peer_ranks = [q for q in range(self.world) if q != self.rank]
+        self._mapped = [(fp4_gemm.ipc_open(everyone[q][0], everyone[q][1], device), everyone[q][1])
+                        for q in self.peer_ranks]
+        self.epoch = 0
+
+    @classmethod
+    def for_group(cls, group, device) -> "PeerFlagBarrier":
+        """The group's barrier, created on first use (a collective call: every rank at once)."""
+        key = (id(group), str(device))
+        b = cls._by_group.get(key)
+        if b is None:
+            b = cls._by_group[key] = cls(group, device)
+        return b
+
+    def wait(self):
+        import fp4_gemm
+        self.epoch += 1
+        fp4_gemm.peer_barrier(self.flags, [p for p, _ in self._mapped], self.peer_ranks, self.rank, self.epoch)
+
+    def close(self):
+        """Unmap the peers' arrays (after the device has drained) and forget the barrier."""
+        import fp4_gemm
+        torch.cuda.synchronize(self.device)
+        for ptr, off in self._mapped:
+            fp4_gemm.ipc_close(ptr, off, self.device)
+        self._mapped = []
+        dist.barrier(group=self.group)  # no peer still maps this rank's array
+        PeerFlagBarrier._by_group.pop((id(self.group), str(self.device)), None)
+
+    @classmethod
+    def close_all(cls):
+        """Close every barrier of this process (before destroy_process_group)."""
+        for b in list(cls._by_group.values()):
+            b.close()
+
+
 def peer_targets(peer_bases: dict, rank: int, world: int, buf: int, cap: int, n: int, start: int) -> list:
     """Device addresses where this rank's first output column lands in every other
     rank's double buffer [2, cap, n] (BF16): buffer `buf`, row 0, column `start`."""
@@ -121,8 +184,10 @@ class ColumnParallelFP4Linear:
     `weight` is the full [N, K] BF16 weight (each rank slices its own rows);
     the output of ``forward`` is the full [M, N] on every rank.  With
     mode "p2p" (the default where it applies) the result is a view of one of
-    two per-layer buffers that the ranks write into each other: it stays
-    valid until the second following ``forward``."""
+    two per-layer buffers that the ranks write into each other: work queued
+    before this rank's next ``forward`` of the layer may read it (the peers
+    write the same buffer again in the forward after that, once this rank
+    has passed the next one's barrier)."""
 
     def __init__(self, weight: torch.Tensor, bias: torch.Tensor = None, group=None, mode: str = "auto"):
         import fp4_gemm
@@ -144,7 +209,7 @@ class ColumnParallelFP4Linear:
         self._bufs = None       # [2, cap, N] BF16, written by every rank
         self._peer_bases = {}   # rank -> (address of its _bufs in this process, IPC offset)
         self._flip = 0
-        self._flag = None
+        self._barrier = None
 
     def uses_p2p(self, m: int) -> bool:
         """Same answer on every rank for the same M (the ranks must agree)."""
@@ -166,7 +231,7 @@ class ColumnParallelFP4Linear:
         self._close_peers()
         cap = ((m + 127) // 128) * 128
         self._bufs = torch.empty(2, cap, self.n, dtype=torch.bfloat16, device=self.device)
-        self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self._barrier = PeerFlagBarrier.for_group(self.group, self.device)
         mine = fp4_gemm.ipc_handle(self._bufs)
         everyone = [None] * self.world
         dist.all_gather_object(everyone, (mine[0], mine[1], cap), group=self.group)
@@ -205,7 +270,7 @@ class ColumnParallelFP4Linear:
             peers = peer_targets(bases, self.rank, self.world, self._flip, cap, self.n, sh.start)
             fp4_gemm.run_cached_peers(x2, self.cache, out[:, sh.start:sh.stop], peers)
         # Every rank's tiles are in every buffer once all ranks have passed this point.
-        dist.all_reduce(self._flag, group=self.group)
+        self._barrier.wait()
         return out.reshape(*lead, self.n)
 
     def free(self):

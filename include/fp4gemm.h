@@ -107,7 +107,8 @@ const char* fp4b_last_error(void);
 
 /* Non-zero if a kernel on the current device gave up on a bounded wait: the
  * first code recorded (GEMM 1 producer, 2 MMA, 3 epilogue, 4 fused-quantize
- * wait; 5 quantizer ring; 7 / 8 the self-test below); clear != 0 resets it.
+ * wait; 5 quantizer ring; 7 / 8 the self-test below; 9 fp4b_mma_rate's final
+ * wait; 10 fp4b_peer_barrier); clear != 0 resets it.
  * Synchronises the device. */
 int fp4b_device_error(int clear);
 
@@ -219,14 +220,28 @@ int fp4b_run_cached_noalloc(const void* A_bf16, int m, int k_in, int lda, const 
  * by the GEMM epilogue itself, to the npeers (1..7) buffers peer_d[] (other
  * GPUs' [.., ldd] BF16 outputs mapped with fp4b_ipc_open_handle, each already
  * offset to this rank's first column) with NVLink stores.  The caller orders
- * the ranks after the call (for example with a one-element all-reduce on the
- * same stream).  m > 128, no C.  D and every peer_d[i] must be 16-byte aligned
+ * the ranks after the call (fp4b_peer_barrier on the same stream, or a
+ * collective).  m > 128, no C.  D and every peer_d[i] must be 16-byte aligned
  * and ldd a multiple of 8 elements (the epilogue stores 16 bytes at a time);
  * otherwise -2 before any device work.  Asynchronous on `stream`; other return
  * codes as fp4b_run_cached_ex. */
 int fp4b_run_cached_peers(const void* A_bf16, int m, int k_in, int lda, const void* cache_handle, int n_out,
                           void* D_bf16, int ldd, void* const* peer_d, int npeers, const void* bias_bf16,
                           void* stream);
+
+/* The ranks' ordering step after fp4b_run_cached_peers (no counterpart in the
+ * reference): one GPU warp release-stores `epoch` into slot my_rank of each
+ * peer's flag array (peer_flags[i], the peer's array of 8 u64 slots mapped with
+ * fp4b_ipc_open_handle), then waits until slot peer_ranks[i] of this rank's own
+ * array `my_flags` holds at least `epoch`.  Call it on the stream of the GEMM,
+ * right after it, with the same epoch on every rank (a per-call counter that
+ * starts at 1 and only grows; the arrays start zeroed and are never reset).
+ * Work queued after it sees every peer's output columns.  The wait gives up
+ * after 10 s, recording 10 in the device error word (fp4b_device_error).
+ * Asynchronous; 0, -1 bad arguments (1..7 peers, ranks 0..7, 8-byte aligned
+ * arrays), -4 launch failure. */
+int fp4b_peer_barrier(const void* my_flags, void* const* peer_flags, const int* peer_ranks, int npeers,
+                      int my_rank, unsigned long long epoch, void* stream);
 
 /* CUDA IPC for the peer buffers (no counterpart in the reference): the 64-byte
  * handle of the allocation holding `ptr` and ptr's offset in it; opening maps

@@ -145,3 +145,27 @@ def test_peer_outputs_must_be_16_byte_aligned(lib):
     # aligned everything: the call goes on to the handle check (NULL here) and fails there instead
     assert call(0x20000, 512, [0x30000, 0x40000]) == -1
     assert b"cache handle" in lib.fp4b_last_error()
+
+
+def test_peer_barrier_rejects_bad_arguments(lib):
+    # fp4b_peer_barrier checks its arguments on the host before any launch.
+    lib.fp4b_last_error.restype = ctypes.c_char_p
+    fn = lib.fp4b_peer_barrier
+    fn.restype = ctypes.c_int
+    vp = ctypes.c_void_p
+    fn.argtypes = [vp, ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_int), ctypes.c_int, ctypes.c_int,
+                   ctypes.c_ulonglong, vp]
+
+    def call(mine, peers, ranks, my_rank, epoch):
+        p = (vp * max(1, len(peers)))(*peers)
+        r = (ctypes.c_int * max(1, len(ranks)))(*ranks)
+        return fn(mine, p, r, len(peers), my_rank, epoch, None)
+
+    assert call(None, [0x1000], [1], 0, 1) == -1            # no flag array
+    assert call(0x2000, [], [], 0, 1) == -1                 # no peers
+    assert call(0x2000, [0x1000], [1], 0, 0) == -1          # epochs start at 1
+    assert call(0x2004, [0x1000], [1], 0, 1) == -1          # misaligned own array
+    assert call(0x2000, [0x1004], [1], 0, 1) == -1          # misaligned peer array
+    assert call(0x2000, [0x1000], [0], 0, 1) == -1          # a peer with this rank's own rank
+    assert call(0x2000, [0x1000] * 8, list(range(1, 9)), 0, 1) == -1  # at most 7 peers
+    assert b"fp4b_peer_barrier" in lib.fp4b_last_error()

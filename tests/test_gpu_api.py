@@ -206,11 +206,19 @@ def test_forward_host_equals_forward(cuda, fp4, m, chunk):
             cache.forward_host(x, chunk_rows=100)
 
 
-@pytest.mark.parametrize("m,n,k", [(2048, 2880, 7680), (200, 300, 384), (384, 1000, 640), (4096, 640, 1024)])
-def test_fused_quantize_gemm_equals_two_kernels(cuda, fp4, monkeypatch, m, n, k):
+@pytest.mark.parametrize("m,n,k,bn", [(2048, 2880, 7680, None), (200, 300, 384, None), (384, 1000, 640, None),
+                                      (4096, 640, 1024, None), (130, 640, 2880, None), (300, 512, 300, None),
+                                      (512, 2880, 2880, "128"), (512, 2880, 2880, "192"), (512, 2880, 2880, "256"),
+                                      (512, 2880, 2880, "320"), (512, 2880, 2880, "384"),
+                                      (4096, 2880, 2880, None)])
+def test_fused_quantize_gemm_equals_two_kernels(cuda, fp4, monkeypatch, m, n, k, bn):
     # With FP4B_FUSE=1 and M > 128 the cached linear quantizes the activations
-    # inside the GEMM kernel; the result must be the two-kernel path's bytes
-    # exactly.
+    # inside the GEMM kernel when its tiles fit in one round of CTA pairs (the
+    # last shape does not: two kernels run); the result must be the
+    # two-kernel path's bytes exactly, for every tile width, ragged M and K,
+    # a K that ends half-way through a 256-wide stage, and repeated launches.
+    if bn:
+        monkeypatch.setenv("FP4B_FORCE_BN", bn)
     x, w, b = W.cached_linear_inputs(m, n, k, seed=23)
     with fp4.FP4WeightCache(w.to(cuda), b.to(cuda)) as cache:
         xd = x.to(cuda)

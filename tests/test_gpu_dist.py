@@ -59,9 +59,13 @@ def _worker(rank, world, port, q):
         dp = D.DataParallelFP4Linear(wd, bd)
         yl = dp.forward(xd[r0:r1], sync=True)
         assert_gemm_close(yl, ref[r0:r1].float(), f"data-parallel rank {rank}")
+        barrier = D.PeerFlagBarrier.for_group(None, dev)
+        assert barrier.epoch >= 4  # one GPU flag barrier per p2p forward, no collective
+        assert fp4_gemm.device_error() == 0
         tp.free()
         dp.free()
         single.free()
+        D.PeerFlagBarrier.close_all()
         torch.cuda.synchronize()
         dist.barrier()
         q.put((rank, "ok"))
