@@ -21,10 +21,10 @@ weak scaling -- every rank runs the full per-GPU workload on its own
 activations, no collective on the data path; the reported value is all ranks'
 FLOPs over the slowest rank's time.  The same line carries config 5 (the
 decoder-layer linear stack, M = 8192) run in every mode on the same ranks:
-"single" (each rank the whole stack alone: the 1-GPU time), "tp_p2p" and
-"tp_nccl" (weights N-sharded, output columns assembled on every rank by the
-GEMM epilogue's NVLink stores or by an NCCL all-gather), and "dp" (rows
-split), with strong-scaling efficiency, the bytes each rank receives per step
+"single" (each rank the whole stack alone: the 1-GPU time), "tp_p2p",
+"tp_epilogue" and "tp_nccl" (weights N-sharded, output columns assembled on
+every rank by copy-engine pushes over NVLink, by the GEMM epilogue's NVLink
+stores, or by an NCCL all-gather), and "dp" (rows split), with strong-scaling efficiency, the bytes each rank receives per step
 and a byte-for-byte check of a column-parallel linear against one GPU
 (`tp_bytes_equal`).  `--impl reference` times the reference's CPU path (its
 own quantizer compiled for the host + fp32 matmul of the dequantized
@@ -311,7 +311,9 @@ def stack_activations(dev, r0: int, r1: int) -> dict:
 def time_stack(mode: str, layers: int, steps: int, warmup: int, ws: int, rank: int, dev) -> float:
     """Milliseconds per stack step (max over ranks).  mode: "single" (this rank
     runs the whole stack alone), "dp" (rows split over the ranks), "tp_p2p" /
-    "tp_nccl" (weights N-sharded, output columns assembled on every rank)."""
+    "tp_epilogue" / "tp_nccl" (weights N-sharded, output columns assembled on
+    every rank by copy-engine pushes, by the GEMM epilogue's stores, or by an
+    NCCL all-gather)."""
     import torch.distributed as dist
 
     import fp4_gemm
@@ -389,7 +391,7 @@ def tp_bytes_equal(ws: int, dev) -> bool:
     single = fp4_gemm.FP4WeightCache(w, b)
     ref = single.forward(x, sync=True)
     ok = True
-    for mode in ("p2p", "nccl"):
+    for mode in ("p2p", "epilogue", "nccl"):
         tp = D.ColumnParallelFP4Linear(w, b, mode=mode)
         ok = ok and bool(torch.equal(tp.forward(x), ref))
         tp.free()
@@ -403,7 +405,7 @@ def stack_report(args, ws: int, rank: int, dev) -> dict:
     """Config 5 in every mode that applies at this world size (see the module docstring)."""
     layers = args.layers
     flops = stack_flops(layers)
-    modes = ["single"] + (["tp_p2p", "tp_nccl", "dp"] if ws > 1 else [])
+    modes = ["single"] + (["tp_p2p", "tp_epilogue", "tp_nccl", "dp"] if ws > 1 else [])
     out = {"workload": f"config 5: {layers} layers x (QKV 2880->5120, O 4096->2880, gate_up 2880->15360, "
                        f"down 7680->2880), M={STACK_M} tokens, weights N(0,0.02) cached as NVFP4, fresh N(0,1) "
                        "activations per linear (quantized every call), no bias",

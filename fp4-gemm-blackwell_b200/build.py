@@ -18,7 +18,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libfp4gemm.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["capi.cu", "quantize.cu", "gemm_sm100.cu", "noalloc.cu", "selftest.cu", "peak.cu", "peer_barrier.cu"]
+SOURCES = ["capi.cu", "quantize.cu", "quantize_units.cu", "gemm_sm100.cu", "noalloc.cu", "selftest.cu", "peak.cu", "peer_barrier.cu"]
 HEADERS = ["fp4b_internal.h", "nvfp4_codec.cuh", "ptx_sm100.cuh", "quantize_core.cuh"]
 
 NVCC_FLAGS = [

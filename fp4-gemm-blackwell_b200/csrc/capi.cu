@@ -41,7 +41,7 @@ struct DeviceState {
     bool initialized = false;
     int M = 0, N = 0, K = 0;
     Buffer a_fp4, a_sf, b_fp4, b_sf;
-    Buffer sync;  // zeroed tile counters of the fused quantize+GEMM kernel
+    Buffer sync;  // zeroed unit counters of the overlapped quantize + GEMM
 };
 
 // g_mu guards the scratch state; launchers run while it is held, so anything
@@ -362,14 +362,14 @@ FP4B_EXPORT int fp4b_run_cached_ex(const void* A, int m, int k_in, int lda, cons
     GemmArgs g{s.a_fp4.ptr, s.a_sf.ptr, c->fp4, c->sf, m, n_out, c->K, m_pad, c->N, C, ldc, D, ldd, bias,
                alpha * c->w_alpha, beta};
     QuantizeArgs q{A, m, k_in, lda, m_pad, c->K, s.a_fp4.ptr, s.a_sf.ptr};
+    g.b_cached = true;  // right behind the activation quantizer
     if (m > 128 && !quantize_check(q) && !gemm_check(g) &&
         reserve_zeroed(s.sync, (size_t)(1 + (m_pad / 128) * ((c->K + 255) / 256)) * sizeof(uint32_t))) {
-        // One kernel quantizes the activations and multiplies (CTA-pair path).
-        const cudaError_t e = gemm_launch_fused(g, q, reinterpret_cast<uint32_t*>(s.sync.ptr), st);
-        if (e != cudaErrorNotSupported) return launch_status(e, "fused quantize+gemm launch");
+        // The quantizer and the GEMM run side by side (CTA-pair path, one round of tiles).
+        const cudaError_t e = gemm_launch_overlapped(g, q, reinterpret_cast<uint32_t*>(s.sync.ptr), st);
+        if (e != cudaErrorNotSupported) return launch_status(e, "overlapped quantize+gemm launch");
     }
     if (int rc = quantize_into(A, m, k_in, lda, s.a_fp4.ptr, s.a_sf.ptr, m_pad, c->K, st)) return rc;
-    g.b_cached = true;
     return gemm_into(g, st);
 }
 
@@ -419,6 +419,17 @@ FP4B_EXPORT int fp4b_run_cached_peers(const void* A, int m, int k_in, int lda, c
         return -2;
     }
     return launch_status(e, "peer gemm launch");
+}
+
+FP4B_EXPORT int fp4b_copy2d(void* dst, long dpitch, const void* src, long spitch, long width_bytes, long height,
+                            void* stream) {
+    if (!dst || !src || width_bytes <= 0 || height <= 0 || dpitch < width_bytes || spitch < width_bytes) {
+        set_last_error("fp4b_copy2d: bad arguments");
+        return -1;
+    }
+    return launch_status(cudaMemcpy2DAsync(dst, (size_t)dpitch, src, (size_t)spitch, (size_t)width_bytes,
+                                           (size_t)height, cudaMemcpyDeviceToDevice, as_stream(stream)),
+                         "fp4b_copy2d");
 }
 
 namespace {

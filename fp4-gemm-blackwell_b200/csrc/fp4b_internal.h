@@ -53,14 +53,27 @@ const char* gemm_check(const GemmArgs& g);
 int gemm_tile_width(long m, long n, long k_pad, int sms);
 cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream);
 
-// Cached linear with the activation quantization inside the GEMM kernel (the
-// CTA-pair path, M > 128, tiles in one round of CTA pairs; opt-in with
-// FP4B_FUSE=1): the kernel quantizes `qa` (whose outputs must be g.a_fp4 /
-// g.a_sf) and multiplies.  `sync_words` is a device array of
+// Overlapped cached linear (CTA-pair path, M > 128, tiles in one round of CTA
+// pairs; opt-in with FP4B_OVERLAP=1): launches the activation quantizer of
+// quantize_units.cu (`qa`, whose outputs must be g.a_fp4 / g.a_sf) and, right
+// behind it, the GEMM, which runs beside the quantizer on the same SMs and
+// waits for the units of A it needs.  `ready` is a device array of
 // 1 + (m_rows_pad / 128) * ceil(k_pad / 256) words that is zero before the
-// first launch; the kernel leaves it zero.  Launches that share `sync_words`
-// must be ordered (same stream).  Returns cudaErrorNotSupported when the fused
-// path does not apply; the caller then runs quantize_launch and gemm_launch.
+// first launch; the GEMM leaves it zero.  Launches that share `ready` must be
+// ordered (same stream).  Returns cudaErrorNotSupported, having launched
+// nothing, when the path does not apply; the caller then runs quantize_launch
+// and gemm_launch.
+cudaError_t gemm_launch_overlapped(const GemmArgs& g, const QuantizeArgs& qa, uint32_t* ready,
+                                   cudaStream_t stream);
+
+// The overlapped path's quantizer (quantize_units.cu): nullptr if `a` suits
+// it (16-byte aligned rows, padded rows a multiple of 64), else a message;
+// its dynamic shared memory for a ring of `ring` 8 KB stages; its launch
+// (`grid` CTAs, one per SM) publishing unit counters into `ready`.
+const char* quantize_units_check(const QuantizeArgs& a);
+int quantize_units_smem_bytes(int ring);
+cudaError_t quantize_units_launch(const QuantizeArgs& a, uint32_t* ready, int ring, int grid, cudaStream_t stream);
+
 // GEMM whose output tile is also stored into `npeers` (1..7) other BF16
 // buffers with the same row stride (other GPUs' memory mapped into this
 // process, each offset to the columns this rank computes): the column-parallel
@@ -68,8 +81,7 @@ cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream);
 // 16-byte aligned; else cudaErrorNotSupported.
 cudaError_t gemm_launch_peers(const GemmArgs& g, void* const* peers, int npeers, cudaStream_t stream);
 
-cudaError_t gemm_launch_fused(const GemmArgs& g, const QuantizeArgs& qa, uint32_t* sync_words,
-                              cudaStream_t stream);
+
 
 // Read-only view of a weight-cache handle created by the C ABI.
 struct CacheView {

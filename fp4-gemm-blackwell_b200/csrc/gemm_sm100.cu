@@ -115,14 +115,11 @@ struct Params {
     int tma_store;  // D written by TMA from shared memory (C unused, D rows 16-byte aligned)
     int bias_vec;   // bias 16-byte aligned: read 8 values per load
     int b_early;    // B and its scales do not depend on the preceding kernel: load them before its completion
-    // Fused activation quantization (pair kernel, FUSED): the kernel quantizes
-    // the BF16 activations described by `q` into a_fp4 / a_sf itself.
-    qcore::QuantParams q;
-    const qcore::QuantTables* qtab;
-    // [a_tiles128][a_stages] units done per 128-row tile of A and K-stage, then
-    // one CTA-exit counter (ready_count = a_tiles128 * a_stages words before it).
+    // Await mode (pair kernel, AWAIT): [a_tiles128][a_stages] units of A
+    // quantized per 128-row tile and K-stage (published by the quantizer running
+    // beside this kernel), then one CTA-exit counter (ready_count words before it).
     uint32_t* ready;
-    int a_groups, a_stages, ready_count;  // 64-row groups of the padded A, K-stages
+    int a_tiles128, a_stages, ready_count;
     // Column-parallel output (pair kernel, TMA-store epilogue): every tile is
     // also written to npeers other [m, ldd] BF16 buffers (other GPUs' memory
     // mapped into this process), each already offset to this rank's columns;
@@ -636,124 +633,17 @@ struct PairCfg {
 
 constexpr uint64_t kAbortDrainNs = 200000;  // after an abort, let issued copies land
 constexpr int kPairThreads = 416;
-constexpr int kPairThreadsFused = 448;  // + the publisher warp
 constexpr int kPairMmaWarp = 8;
 constexpr int kPairFirstProducer = 9;
 
-// Fused mode (FUSED): the kernel quantizes its BF16 activations itself, for
-// problems whose tiles fit in one round of CTA pairs, so that the epilogue
-// warps are idle while the MMAs run.  The padded rows of A are cut into units
-// of 64 rows x one 256-wide K-stage (16 blocks of 16), ordered K-stage by
-// K-stage: unit u covers K-stage u / R of the 64-row group u % R (R = rows_pad
-// / 64).  CTA c of the grid quantizes units c, c + G, c + 2G, ... with its
-// eight epilogue warps: warp w takes rows [8w, 8w + 8) of the unit and lane l
-// the block kb = 16 ks + (l & 15) of rows 2j + (l >> 4), j = 0..3, so each
-// half warp reads 512 contiguous bytes of one row, and four consecutive lanes
-// hold four consecutive blocks of a row (one 4-byte scale store).  The loads
-// of the CTA's next unit are in flight while the current unit is quantized.
-// Once a unit's codes and scales are stored, the eight warps and a publisher
-// warp meet at a named barrier; the publisher, which has no loads of its own
-// in flight (a fence would wait for them), fences and adds one to the counter
-// of the unit's 128-row tile and K-stage.  The A and scale-A producers of a
-// stage wait (bounded) until their tile's counter for that stage reaches 2.
+// Await mode (AWAIT, the overlapped cached linear): the activation quantizer
+// (quantize_units.cu) runs beside this kernel on the same SMs and publishes,
+// for every 128-row tile of A and 256-wide K-stage, a counter that reaches 2
+// once both of its 64-row units are stored.  The A and scale-A producers wait
+// (bounded) for their tile's counter of each stage instead of for the whole
+// quantizer grid, and the MMA and producer warps skip the programmatic wait
+// altogether; only the epilogue warps wait for the quantizer to complete.
 // The last CTA to exit zeroes the counters for the next launch.
-constexpr int kUnitRows = 64;
-constexpr int kUnitBlocks = 4;           // blocks per lane per unit
-constexpr uint32_t kUnitBarrier = 2;      // named barrier id (1 is the epilogue warps' own)
-constexpr int kPairPublisherWarp = 13;   // fused kernel only
-
-__device__ __forceinline__ void load_block_rk(const qcore::QuantParams& q, uint32_t r, uint32_t kb,
-                                              uint32_t (&w)[8]) {
-    const uint32_t c0 = kb * kSfVec;
-    if (kb >= q.nsb) {  // past the padded K of a half-width last K-stage: not stored
-#pragma unroll
-        for (int i = 0; i < 8; ++i) w[i] = 0u;
-    } else if (q.vec_ok && r < q.rows && c0 + kSfVec <= q.cols) {
-        const uint4* g = reinterpret_cast<const uint4*>(q.src + (size_t)r * q.ld + c0);
-        const uint4 v0 = __ldcs(g);
-        const uint4 v1 = __ldcs(g + 1);
-        w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
-        w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
-    } else {
-        // Ragged edge, padding rows or columns, unaligned rows: element loads, zeros outside.
-#pragma unroll
-        for (int i = 0; i < 8; ++i) w[i] = qcore::load_pair(q.src, q.ld, q.rows, q.cols, r, c0 + 2 * i);
-    }
-}
-
-// Row and block of this lane's j-th block of unit u.
-__device__ __forceinline__ void unit_block(uint32_t u, uint32_t R, int warp, int lane, int j, uint32_t& r,
-                                           uint32_t& kb) {
-    const uint32_t ks = u / R, grp = u - ks * R;
-    r = grp * kUnitRows + 8u * (uint32_t)warp + 2u * (uint32_t)j + ((uint32_t)lane >> 4);
-    kb = ks * 16u + ((uint32_t)lane & 15u);
-}
-
-__device__ __forceinline__ void load_unit(const qcore::QuantParams& q, uint32_t u, uint32_t R, int warp, int lane,
-                                          uint32_t (&w)[kUnitBlocks][8]) {
-#pragma unroll
-    for (int j = 0; j < kUnitBlocks; ++j) {
-        uint32_t r, kb;
-        unit_block(u, R, warp, lane, j, r, kb);
-        load_block_rk(q, r, kb, w[j]);
-    }
-}
-
-__device__ __forceinline__ void store_unit(const qcore::QuantParams& q, uint32_t u, uint32_t R, int warp, int lane,
-                                           const uint32_t (&w)[kUnitBlocks][8], const qcore::SmemTables& tab) {
-#pragma unroll
-    for (int j = 0; j < kUnitBlocks; ++j) {
-        uint32_t r, kb;
-        unit_block(u, R, warp, lane, j, r, kb);
-        qcore::quantize_and_store(q, r * q.nsb + kb, kb < q.nsb ? q.total : 0u, w[j], r, kb, (uint32_t)lane, tab);
-    }
-}
-
-// The eight quantizing warps: every unit of this CTA, one named barrier per
-// unit (the publisher takes the same number).
-template <int kWarps>
-__device__ __forceinline__ void quantize_units(const Params& p, const qcore::SmemTables& tab, int warp, int lane) {
-    const qcore::QuantParams& q = p.q;
-    const uint32_t R = (uint32_t)p.a_groups, U = R * (uint32_t)p.a_stages, G = gridDim.x;
-    uint32_t u = blockIdx.x;
-    if (u >= U) return;
-    uint32_t wa[kUnitBlocks][8], wb[kUnitBlocks][8];
-    load_unit(q, u, R, warp, lane, wa);
-    for (;;) {
-        // Two register sets used in turn: the next unit's loads are in flight
-        // while the current one is quantized.
-        const uint32_t u1 = u + G;
-        if (u1 < U) load_unit(q, u1, R, warp, lane, wb);
-        store_unit(q, u, R, warp, lane, wa, tab);
-        __syncwarp();
-        ptx::named_barrier(kUnitBarrier, (kWarps + 1) * 32);
-        if (u1 >= U) break;
-        const uint32_t u2 = u1 + G;
-        if (u2 < U) load_unit(q, u2, R, warp, lane, wa);
-        store_unit(q, u1, R, warp, lane, wb, tab);
-        __syncwarp();
-        ptx::named_barrier(kUnitBarrier, (kWarps + 1) * 32);
-        if (u2 >= U) break;
-        u = u2;
-    }
-}
-
-// The publisher warp: after each unit's barrier, make the unit's stores
-// visible to every CTA's TMA loads and count the unit.
-template <int kWarps>
-__device__ __forceinline__ void publish_units(const Params& p, int lane) {
-    const uint32_t R = (uint32_t)p.a_groups, U = R * (uint32_t)p.a_stages;
-    for (uint32_t u = blockIdx.x; u < U; u += gridDim.x) {
-        ptx::named_barrier(kUnitBarrier, (kWarps + 1) * 32);
-        if (lane == 0) {
-            const uint32_t ks = u / R, grp = u - ks * R;
-            ptx::fence_proxy_async_global();
-            __threadfence();
-            atomicAdd(p.ready + (grp >> 1) * (uint32_t)p.a_stages + ks, 1u);
-        }
-        __syncwarp();
-    }
-}
 
 // Epilogue of a CTA pair's last tile by a team of warps per TMEM lane
 // quadrant q: the two epilogue warps q and q + 4 (members 0, 1) and the warps
@@ -789,8 +679,8 @@ __device__ __forceinline__ void team_epilogue(const Params& p, const CUtensorMap
     }
 }
 
-template <int BN, int STAGES, bool FUSED, int NSUB, int BN1>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FUSED ? kPairThreadsFused : kPairThreads, 1)
+template <int BN, int STAGES, bool AWAIT, int NSUB, int BN1>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     nvf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_b1,
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
@@ -861,17 +751,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FUSED ? kPairThreads
     // stage's byte count; the phase still needs that arrival).  Every other
     // role touches global memory only after the quantizer has completed; the
     // producers' last-tile epilogue work follows the MMA warp's, which does.
+    // In await mode the quantizer is still running: the A producers wait for
+    // its counters instead, and the MMA and producer warps do not wait for it.
     const bool early_b = p.b_early && warp >= kPairFirstProducer && ((warp - kPairFirstProducer) & 1) == 1;
-    if (!early_b) ptx::grid_dependency_wait();
+    if (!early_b && !(AWAIT && warp >= kPairMmaWarp)) ptx::grid_dependency_wait();
     // The kernel after this one (the next quantizer) may be scheduled on SMs
     // this grid leaves; it waits for this grid to complete before it reads or
     // writes global memory.
     ptx::launch_dependents();
 
-    if (FUSED && warp == kPairPublisherWarp) {
-        // ------------------------------------------------------------ publisher (fused mode)
-        publish_units<kPairEpiWarps>(p, lane);
-    } else if (warp >= kPairFirstProducer) {
+    if (warp >= kPairFirstProducer) {
         // ------------------------------------------------------------ producers (both CTAs)
         const int role = warp - kPairFirstProducer;  // 0 A, 1 B, 2 scale-A, 3 scale-B
         const uint32_t full0 = ptx::map_to_cta(ptx::smem_u32(full), 0);
@@ -902,11 +791,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FUSED ? kPairThreads
                     stop = true;
                     break;
                 }
-                if constexpr (FUSED) {
+                if constexpr (AWAIT) {
                     // A CTA whose 128 rows lie wholly past the padded rows of A (the
                     // second half of a last 256-row tile when rows_pad % 256 == 128)
                     // has no units to wait for: its TMA boxes read zeros.
-                    if ((role == 0 || role == 2) && 2 * m_tile + (int)rank < (p.a_groups >> 1)) {
+                    if ((role == 0 || role == 2) && 2 * m_tile + (int)rank < p.a_tiles128) {
                         // Both 64-row units of this CTA's 128 rows of A for this K-stage
                         // are quantized and visible to TMA.
                         bool ok = true;
@@ -1044,14 +933,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FUSED ? kPairThreads
         const uint32_t acc_empty0 = ptx::map_to_cta(ptx::smem_u32(acc_empty), 0);
         uint8_t* epi = sEpi + warp * 2048;
         uint4* wbias = sBias + warp * (TW / 16);
-        if constexpr (FUSED) {
-            // The quantizer tables live in the (not yet used) epilogue staging buffers.
-            static_assert(C::EPI_BYTES >= qcore::kSmemTableBytes, "tables must fit the staging buffers");
-            const qcore::SmemTables tab = qcore::copy_tables(p.qtab, sEpi, threadIdx.x, kPairEpiWarps * 32);
-            ptx::named_barrier(1, kPairEpiWarps * 32);
-            quantize_units<kPairEpiWarps>(p, tab, warp, lane);
-            ptx::named_barrier(1, kPairEpiWarps * 32);  // tables no longer read: buffers free
-        }
         int chunk_iter = 0;
         int tile_iter = 0;
         for (int t = pair; t < p.num_tiles; t += npairs, ++tile_iter) {
@@ -1149,7 +1030,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FUSED ? kPairThreads
         }
     }
 
-    if (warp >= kPairMmaWarp && warp < kPairPublisherWarp && !__any_sync(0xffffffffu, aborted(s_abort))) {
+    if (warp >= kPairMmaWarp && !__any_sync(0xffffffffu, aborted(s_abort))) {
         // -------------------------------------------- MMA and producer warps: help with the last tile
         const int q = warp & 3;
         const int ti = warp == kPairThreads / 32 - 1 ? 3 : 2;  // warp 12 is quadrant 0's fourth member
@@ -1194,7 +1075,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FUSED ? kPairThreads
             }
         }
     }
-    if constexpr (FUSED) {
+    if constexpr (AWAIT) {
         // The last CTA to get here (all producers are past their waits) zeroes
         // the unit counters for the next launch.
         if (threadIdx.x == 0) {
@@ -1343,11 +1224,14 @@ int max_pairs(K kernel, int smem, int sms, int threads) {
     return c;
 }
 
-template <int BN, int STAGES, bool FUSED = false, int NSUB = 1, int BN1 = BN>
+// Shared memory of one SM (233472 bytes on B200) minus a CTA's reserved 1 KB.
+constexpr int kSmemPerSm = 233472;
+
+template <int BN, int STAGES, bool AWAIT = false, int NSUB = 1, int BN1 = BN>
 cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const QuantizeArgs* qa = nullptr,
-                        uint32_t* sync_words = nullptr, void* const* peers = nullptr, int npeers = 0) {
+                        uint32_t* ready = nullptr, void* const* peers = nullptr, int npeers = 0) {
     using C = PairCfg<BN, STAGES, NSUB, BN1>;
-    auto kernel = nvf4_gemm_pair_kernel<BN, STAGES, FUSED, NSUB, BN1>;
+    auto kernel = nvf4_gemm_pair_kernel<BN, STAGES, AWAIT, NSUB, BN1>;
     static std::once_flag attr_once[64];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1375,22 +1259,30 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const Q
             if (!make_output_map(&pm.map[i], peers[i], g.m, g.n_out, g.ldd)) return cudaErrorNotSupported;
         p.npeers = npeers;
     }
-    constexpr int threads = FUSED ? kPairThreadsFused : kPairThreads;
-    const int pairs = max_pairs(kernel, C::SMEM_BYTES, sms, threads);
-    if constexpr (FUSED) {
-        p.qtab = quant_tables_device();
-        if (!p.qtab || !qa || !sync_words) return cudaErrorInvalidValue;
-        // One round of tiles only: the epilogue warps quantize before their first epilogue.
-        if (p.num_tiles > pairs) return cudaErrorNotSupported;
-        p.q = make_quant_params(*qa);
-        p.ready = sync_words;
-        p.a_groups = (int)(g.m_rows_pad / kUnitRows);
-        p.a_stages = (int)((g.k_pad + 255) / 256);
-        p.ready_count = (int)(g.m_rows_pad / 128) * p.a_stages;
-    }
+    const int pairs = max_pairs(kernel, C::SMEM_BYTES, sms, kPairThreads);
     const int grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);
-    return launch_dependent(kernel, dim3(grid), dim3(threads), C::SMEM_BYTES, stream, ma, mb, mb1, msa, msb, md, p,
-                            pm);
+    if constexpr (AWAIT) {
+        if (!qa || !ready) return cudaErrorInvalidValue;
+        // One round of tiles, and room beside this kernel's CTA on an SM for a
+        // quantizer CTA with at least 3 stages of 8 KB; else two kernels run.
+        const int ring_room = kSmemPerSm - C::SMEM_BYTES - 2 * 1024 - quantize_units_smem_bytes(0);
+        const int ring = ring_room / 8192 > 8 ? 8 : ring_room / 8192;
+        if (p.num_tiles > pairs || ring < 3) return cudaErrorNotSupported;
+        p.ready = ready;
+        p.a_tiles128 = (int)(g.m_rows_pad / 128);
+        p.a_stages = (int)((g.k_pad + 255) / 256);
+        p.ready_count = p.a_tiles128 * p.a_stages;
+        // The quantizer first (one CTA per SM), then this kernel behind it.
+        const cudaError_t e = quantize_units_launch(*qa, ready, ring, sms, stream);
+        if (e != cudaSuccess) return e;
+        const cudaError_t e2 = launch_dependent(kernel, dim3(grid), dim3(kPairThreads), C::SMEM_BYTES, stream, ma,
+                                                mb, mb1, msa, msb, md, p, pm);
+        if (e2 != cudaSuccess)  // the quantizer ran alone: leave the counters zero for the next launch
+            cudaMemsetAsync(ready, 0, (size_t)(p.ready_count + 1) * sizeof(uint32_t), stream);
+        return e2;
+    }
+    return launch_dependent(kernel, dim3(grid), dim3(kPairThreads), C::SMEM_BYTES, stream, ma, mb, mb1, msa, msb, md,
+                            p, pm);
 }
 
 template <int BN, int STAGES, int CHUNKS>
@@ -1469,26 +1361,32 @@ int choose_bn_pair(long m, long n, long k_pad, int sms) {
 
 }  // namespace
 
-cudaError_t gemm_launch_fused(const GemmArgs& g, const QuantizeArgs& qa, uint32_t* sync_words,
-                              cudaStream_t stream) {
-    // Opt-in for now (FP4B_FUSE=1); problems whose tiles need more than one
-    // round of CTA pairs return cudaErrorNotSupported (two kernels instead).
-    const char* env = getenv("FP4B_FUSE");
+cudaError_t gemm_launch_overlapped(const GemmArgs& g, const QuantizeArgs& qa, uint32_t* ready, cudaStream_t stream) {
+    // Opt-in (FP4B_OVERLAP=1).  On B200 the quantizer CTA that fits beside a
+    // GEMM CTA (at most ~12 K registers: four quantizing warps) cannot hide the
+    // latency of its per-block work: alone it takes 28.8 us for the headline's
+    // 2048 x 7680 activations (10.6 us for the standalone kernel with 40 warps
+    // per SM), and the overlapped step took 68 us against 30.4 us for the two
+    // kernels in turn.  Bytes are identical either way.
+    const char* env = getenv("FP4B_OVERLAP");
     if (!env || atoi(env) == 0 || g.m <= kBM || (getenv("FP4B_PAIR") && atoi(getenv("FP4B_PAIR")) == 0))
         return cudaErrorNotSupported;
     if (qa.rows_pad != g.m_rows_pad || qa.k_pad != g.k_pad || qa.fp4 != g.a_fp4 || qa.sf != g.a_sf)
         return cudaErrorInvalidValue;
+    if (quantize_units_check(qa)) return cudaErrorNotSupported;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const char* force = getenv("FP4B_FORCE_BN");
     const int bn = force ? atoi(force) : choose_bn_pair(g.m, g.n_out, g.k_pad, sms);
+    // One stage fewer than the two-kernel instantiations, so that a quantizer
+    // CTA fits beside the GEMM's CTA on every SM.
     switch (bn) {
-        case 256: return launch_pair<256, 5, true>(g, stream, sms, &qa, sync_words);
-        case 192: return launch_pair<192, 6, true>(g, stream, sms, &qa, sync_words);
-        case 128: return launch_pair<128, 7, true>(g, stream, sms, &qa, sync_words);
-        case 384: return launch_pair<192, 4, true, 2>(g, stream, sms, &qa, sync_words);
-        case 320: return launch_pair<128, 4, true, 2, 192>(g, stream, sms, &qa, sync_words);
+        case 256: return launch_pair<256, 4, true>(g, stream, sms, &qa, ready);
+        case 192: return launch_pair<192, 4, true>(g, stream, sms, &qa, ready);
+        case 128: return launch_pair<128, 5, true>(g, stream, sms, &qa, ready);
+        case 384: return launch_pair<192, 3, true, 2>(g, stream, sms, &qa, ready);
+        case 320: return launch_pair<128, 3, true, 2, 192>(g, stream, sms, &qa, ready);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -11,7 +11,7 @@
 //     bit patterns, built on the host with IEEE division; reciprocal table;
 //   * E2M1 rounding by the hardware conversion (cvt.rn.satfinite.e2m1x2)
 //     applied to a stand-in for each scaled value that is never a tie and
-//     rounds to the reference's code (e2m1_stand_in in quantize_core.cuh), so
+//     rounds to the reference's code (pack8_e2m1 in quantize_core.cuh), so
 //     the reference's strict-< nearest-value scan (ties to the lower code,
 //     sign for any value < 0) is reproduced bit for bit; blocks with
 //     |x|max >= 2^30, Inf or NaN take a literal scan instead;

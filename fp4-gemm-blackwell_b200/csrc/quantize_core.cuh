@@ -70,21 +70,39 @@ inline void make_fast_div(uint32_t d, uint32_t* mul, uint32_t* shift) {
 // the sign for any v < 0 (fp4_gemm_lib.cu:110-124).  The hardware conversion
 // (cvt.rn.satfinite.e2m1x2.f32) rounds to nearest even, which differs only on
 // ties (0.75, 1.75 and 3.5 go up) and on -0.  So it is applied to a stand-in
-// for v that is never a tie and rounds like v under the reference's rule:
-//   * v = fma(x, inv, +0) is RN(x * inv), except that -0 becomes +0;
-//   * with b the bits of v, (b - 1) | 1 is b itself when b is odd (not a tie:
-//     ties have at least 21 trailing zero bits) and otherwise the float one
-//     ulp closer to zero, which has the same nearest value as v unless v is a
-//     tie, where it has the lower one; the sign is unchanged;
-//   * max(b, 1) maps +0 to the smallest denormal, which converts to +0.
-__device__ __forceinline__ float e2m1_stand_in(float x, float inv) {
-    const uint32_t b = __float_as_uint(__fmaf_rn(x, inv, 0.0f));
-    return __uint_as_float((max(b, 1u) - 1u) | 1u);
+// for v = RN(x * inv) that is never a tie and rounds like v under the
+// reference's rule:
+//   * v' = RN(x * inv + 2^-149), two elements per fma.rn.f32x2.  For the
+//     fast path's inputs this has the reference's code: a zero becomes 2^-149
+//     (code 0, as the reference gives for +0 and -0); every non-zero product
+//     has |x * inv| >= 2^-142, keeps its sign and, when it is not exactly
+//     halfway between two floats, rounds to v; the products that are exactly
+//     halfway (23,720 of all BF16 x and scale reciprocals) move by one ulp
+//     without changing the nearest E2M1 value (checked exhaustively in
+//     tests/test_fast_path_model.py);
+//   * with b the bits of v' (never 0), (b - 1) | 1 is b itself when b is odd
+//     (not a tie: ties have at least 21 trailing zero bits) and otherwise the
+//     float one ulp closer to zero, which has the same nearest value as v'
+//     unless v' is a tie, where it has the lower one; the sign is unchanged.
+constexpr unsigned long long kTinyPair = 0x0000000100000001ull;  // (2^-149, 2^-149)
+
+__device__ __forceinline__ unsigned long long scaled_pair(uint32_t w, unsigned long long inv2) {
+    // w holds two BF16 values, the even element in the low half.
+    const unsigned long long x2 = ((unsigned long long)(w & 0xFFFF0000u) << 32) | (unsigned long long)(w << 16);
+    unsigned long long v2;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(v2) : "l"(x2), "l"(inv2), "l"(kTinyPair));
+    return v2;
 }
+
+__device__ __forceinline__ float stand_in_bits(uint32_t b) { return __uint_as_float((b - 1u) | 1u); }
 
 // Eight elements (four packed BF16 pairs, low element first) -> one word of
 // eight E2M1 codes, element 2i in the low nibble of byte i.
 __device__ __forceinline__ uint32_t pack8_e2m1(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, float inv) {
+    const unsigned long long inv2 =
+        ((unsigned long long)__float_as_uint(inv) << 32) | (unsigned long long)__float_as_uint(inv);
+    const unsigned long long v0 = scaled_pair(w0, inv2), v1 = scaled_pair(w1, inv2);
+    const unsigned long long v2 = scaled_pair(w2, inv2), v3 = scaled_pair(w3, inv2);
     uint32_t out;
     asm("{\n"
         ".reg .b8 b0, b1, b2, b3;\n"
@@ -95,14 +113,10 @@ __device__ __forceinline__ uint32_t pack8_e2m1(uint32_t w0, uint32_t w1, uint32_
         "mov.b32 %0, {b0, b1, b2, b3};\n"
         "}"
         : "=r"(out)
-        : "f"(e2m1_stand_in(__uint_as_float(w0 << 16), inv)),
-          "f"(e2m1_stand_in(__uint_as_float(w0 & 0xFFFF0000u), inv)),
-          "f"(e2m1_stand_in(__uint_as_float(w1 << 16), inv)),
-          "f"(e2m1_stand_in(__uint_as_float(w1 & 0xFFFF0000u), inv)),
-          "f"(e2m1_stand_in(__uint_as_float(w2 << 16), inv)),
-          "f"(e2m1_stand_in(__uint_as_float(w2 & 0xFFFF0000u), inv)),
-          "f"(e2m1_stand_in(__uint_as_float(w3 << 16), inv)),
-          "f"(e2m1_stand_in(__uint_as_float(w3 & 0xFFFF0000u), inv)));
+        : "f"(stand_in_bits((uint32_t)v0)), "f"(stand_in_bits((uint32_t)(v0 >> 32))),
+          "f"(stand_in_bits((uint32_t)v1)), "f"(stand_in_bits((uint32_t)(v1 >> 32))),
+          "f"(stand_in_bits((uint32_t)v2)), "f"(stand_in_bits((uint32_t)(v2 >> 32))),
+          "f"(stand_in_bits((uint32_t)v3)), "f"(stand_in_bits((uint32_t)(v3 >> 32))));
     return out;
 }
 

@@ -83,6 +83,7 @@ _bind("fp4b_ipc_open_handle", _vp, [ctypes.c_char_p, ctypes.c_long])
 _bind("fp4b_ipc_close", _i, [_vp, ctypes.c_long])
 _bind("fp4b_mma_rate", _i, [_i, _i, _i, _i, _i, ctypes.POINTER(_i), _vp])
 _bind("fp4b_peer_barrier", _i, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_i), _i, _i, ctypes.c_ulonglong, _vp])
+_bind("fp4b_copy2d", _i, [_vp, ctypes.c_long, _vp, ctypes.c_long, ctypes.c_long, ctypes.c_long, _vp])
 
 # Query scale factor vector size
 SF_VEC_SIZE = _lib.fp4_gemm_sf_vec_size()
@@ -673,6 +674,32 @@ def peer_barrier(my_flags: torch.Tensor, peer_flag_ptrs, peer_ranks, my_rank: in
         rc = _lib.fp4b_peer_barrier(my_flags.data_ptr(), ptrs, ranks, n, my_rank, epoch, _stream_ptr(my_flags.device))
     if rc != 0:
         raise RuntimeError(f"fp4b_peer_barrier failed with error code {rc} ({_last_error()})")
+
+
+def copy2d(dst: int, dpitch: int, src: int, spitch: int, width_bytes: int, height: int, device) -> None:
+    """Queue a strided device-to-device copy (fp4b_copy2d) on the current stream of `device`."""
+    with torch.cuda.device(device):
+        rc = _lib.fp4b_copy2d(dst, dpitch, src, spitch, width_bytes, height, _stream_ptr(device))
+    if rc != 0:
+        raise RuntimeError(f"fp4b_copy2d failed with error code {rc} ({_last_error()})")
+
+
+def run_cached_into(x: torch.Tensor, cache: "FP4WeightCache", out: torch.Tensor) -> None:
+    """x [M, K] @ cache^T (+ cache.bias, fused when BF16) written into `out` [M, cols], which may be a
+    column slice of a wider buffer (unit column stride, any row stride).  Asynchronous."""
+    x2, lda = _rows_view(x)
+    m, k = x2.shape
+    bias = cache.bias
+    b_ptr = bias.reshape(-1).data_ptr() if (bias is not None and bias.is_cuda and bias.dtype == torch.bfloat16) else None
+    if bias is not None and b_ptr is None:
+        raise ValueError("run_cached_into fuses the bias: it must be a BF16 CUDA tensor")
+    if out.dim() != 2 or out.stride(1) != 1 or out.shape[0] != m:
+        raise ValueError("out must be a 2-D [M, cols] view with unit column stride")
+    with torch.cuda.device(x2.device):
+        rc = _lib.fp4b_run_cached_ex(x2.data_ptr(), m, k, lda, cache._handle, out.shape[1], None, 0, out.data_ptr(),
+                                     out.stride(0), b_ptr, 1.0, 0.0, _stream_ptr(x2.device))
+    if rc != 0:
+        raise RuntimeError(f"fp4_gemm_run_cached failed with error code {rc} ({_last_error()})")
 
 
 def run_cached_peers(x: torch.Tensor, cache: "FP4WeightCache", out: torch.Tensor, peer_ptrs) -> None:

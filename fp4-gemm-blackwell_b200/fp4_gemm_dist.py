@@ -11,16 +11,20 @@ single-GPU kernels of ``fp4_gemm``:
   and keeps only its 128-row slice of W (the same bytes as that slice of the
   full cache, because quantization is row-local and scale atoms cover 128
   rows).  Each rank computes its output columns and the result is assembled
-  as [M, N] on every rank, in one of two ways:
-    - "p2p": the GEMM epilogue itself stores every output tile into the [M, N]
-      buffers of all ranks (CUDA IPC mappings of the peers' buffers, NVLink
-      stores), then a flag barrier on the GPU (``PeerFlagBarrier``: one warp
-      signals every peer and waits for every peer's signal) orders the ranks.
-      No gather buffer, no re-layout, no collective; the transfer overlaps the
-      tiles.
+  as [M, N] on every rank, in one of three ways:
+    - "p2p" (the default): every rank's [M, N] buffer is mapped by every other
+      rank (CUDA IPC).  The rank's GEMM writes its columns into its own
+      buffer in row chunks, and a side stream pushes each finished chunk to
+      every peer's buffer with a strided copy-engine copy over NVLink while
+      the next chunk is computed; a flag barrier on the GPU
+      (``PeerFlagBarrier``: one warp signals every peer and waits for every
+      peer's signal) then orders the ranks.  No gather buffer, no re-layout,
+      no collective, and the GEMM runs at its single-GPU speed.
+    - "epilogue": the GEMM epilogue itself stores every output tile into all
+      ranks' buffers (TMA bulk stores over NVLink), then the flag barrier.
+      Needs M > 128 (the CTA-pair kernel) and N a multiple of 8.
     - "nccl": one NCCL all-gather of equal-size, zero-padded slices and a
-      re-layout.  Used when "p2p" does not apply (M <= 128, N not a multiple
-      of 8, a single rank) or when asked for.
+      re-layout.
 
 Host logic (shard plans, gather and re-layout) is separated from the GPU
 kernels so it can be tested with ``gloo`` process groups on CPU.
@@ -178,6 +182,17 @@ def peer_targets(peer_bases: dict, rank: int, world: int, buf: int, cap: int, n:
     return [peer_bases[q] + 2 * (buf * cap * n + start) for q in range(world) if q != rank]
 
 
+_COPY_STREAMS = {}  # device -> side stream of the p2p mode's peer copies
+
+
+def row_chunks(m: int, min_rows: int = 1024, max_chunks: int = 4) -> list:
+    """Row ranges [r0, r1) of the p2p mode's GEMM chunks: at most max_chunks,
+    each at least min_rows (a multiple of 128) except the last."""
+    size = max(min_rows, -(-m // max_chunks))
+    size = -(-size // TILE) * TILE
+    return [(r0, min(m, r0 + size)) for r0 in range(0, m, size)]
+
+
 class ColumnParallelFP4Linear:
     """N-sharded weight cache; the output columns of all ranks are assembled.
 
@@ -191,8 +206,8 @@ class ColumnParallelFP4Linear:
 
     def __init__(self, weight: torch.Tensor, bias: torch.Tensor = None, group=None, mode: str = "auto"):
         import fp4_gemm
-        if mode not in ("auto", "p2p", "nccl"):
-            raise ValueError("mode must be 'auto', 'p2p' or 'nccl'")
+        if mode not in ("auto", "p2p", "epilogue", "nccl"):
+            raise ValueError("mode must be 'auto', 'p2p', 'epilogue' or 'nccl'")
         self.group = group
         self.mode = mode
         self.world = dist.get_world_size(group)
@@ -212,10 +227,14 @@ class ColumnParallelFP4Linear:
         self._barrier = None
 
     def uses_p2p(self, m: int) -> bool:
-        """Same answer on every rank for the same M (the ranks must agree)."""
-        if self.mode == "nccl" or self.world == 1:
+        """Whether a forward of M rows assembles through the mapped buffers ("p2p"
+        or "epilogue"); the same answer on every rank for the same M (the ranks
+        must agree)."""
+        if self.mode == "nccl" or self.world == 1 or self.device.type != "cuda" or not self._bias_ok or m <= 0:
             return False
-        return m > 128 and self.n % 8 == 0 and self.device.type == "cuda" and self._bias_ok
+        if self.mode == "epilogue":
+            return m > 128 and self.n % 8 == 0
+        return True
 
     def _ensure_buffers(self, m: int):
         import fp4_gemm
@@ -265,12 +284,32 @@ class ColumnParallelFP4Linear:
         cap = self._bufs.shape[1]
         out = self._bufs[self._flip, :m]
         sh = self.shards[self.rank]
+        bases = {q: b for q, (b, _) in self._peer_bases.items()}
+        if self.mode == "epilogue":
+            if sh.cols > 0:
+                peers = peer_targets(bases, self.rank, self.world, self._flip, cap, self.n, sh.start)
+                fp4_gemm.run_cached_peers(x2, self.cache, out[:, sh.start:sh.stop], peers)
+            # Every rank's tiles are in every buffer once all ranks have passed this point.
+            self._barrier.wait()
+            return out.reshape(*lead, self.n)
+        cur = torch.cuda.current_stream(self.device)
+        side = _COPY_STREAMS.get(self.device)
+        if side is None:
+            side = _COPY_STREAMS[self.device] = torch.cuda.Stream(self.device)
+        side.wait_stream(cur)
         if sh.cols > 0:
-            bases = {q: b for q, (b, _) in self._peer_bases.items()}
-            peers = peer_targets(bases, self.rank, self.world, self._flip, cap, self.n, sh.start)
-            fp4_gemm.run_cached_peers(x2, self.cache, out[:, sh.start:sh.stop], peers)
-        # Every rank's tiles are in every buffer once all ranks have passed this point.
-        self._barrier.wait()
+            pitch = 2 * self.n
+            for r0, r1 in row_chunks(m):
+                fp4_gemm.run_cached_into(x2[r0:r1], self.cache, out[r0:r1, sh.start:sh.stop])
+                side.wait_stream(cur)
+                src = out[r0, sh.start:].data_ptr()
+                with torch.cuda.stream(side):
+                    for dst in peer_targets(bases, self.rank, self.world, self._flip, cap, self.n, sh.start):
+                        fp4_gemm.copy2d(dst + r0 * pitch, pitch, src, pitch, 2 * sh.cols, r1 - r0, self.device)
+        with torch.cuda.stream(side):
+            # After this rank's copies; every peer's columns are here once it completes.
+            self._barrier.wait()
+        cur.wait_stream(side)
         return out.reshape(*lead, self.n)
 
     def free(self):

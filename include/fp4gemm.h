@@ -243,6 +243,14 @@ int fp4b_run_cached_peers(const void* A_bf16, int m, int k_in, int lda, const vo
 int fp4b_peer_barrier(const void* my_flags, void* const* peer_flags, const int* peer_ranks, int npeers,
                       int my_rank, unsigned long long epoch, void* stream);
 
+/* One strided device-to-device copy (cudaMemcpy2DAsync): `height` rows of
+ * `width_bytes`, row pitches in bytes; either side may be another GPU's
+ * memory mapped with fp4b_ipc_open_handle, in which case the copy engine moves
+ * it over NVLink.  The column-parallel linear pushes its output columns to the
+ * other ranks with it (no counterpart in the reference).  Asynchronous on
+ * `stream`; 0, -1 bad arguments, -4 failure. */
+int fp4b_copy2d(void* dst, long dpitch, const void* src, long spitch, long width_bytes, long height, void* stream);
+
 /* CUDA IPC for the peer buffers (no counterpart in the reference): the 64-byte
  * handle of the allocation holding `ptr` and ptr's offset in it; opening maps
  * another process's allocation into this one and returns base + offset. */

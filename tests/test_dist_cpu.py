@@ -128,3 +128,13 @@ def test_rank_that_leaves_ends_the_survivors_collective_with_an_error():
     assert codes == [0, 0], f"rank exit codes {codes}"
     rank, outcome = q.get(timeout=10)
     assert rank == 0 and outcome != "returned", outcome
+
+
+def test_row_chunks_partition_rows():
+    # The p2p mode's GEMM chunks: contiguous, cover [0, M), at most 4, 128-row
+    # multiples of at least 1024 rows except the last.
+    for m in (1, 100, 1024, 2048, 2304, 8192, 8200, 20000):
+        ch = D.row_chunks(m)
+        assert ch[0][0] == 0 and ch[-1][1] == m and len(ch) <= 4
+        for (a0, a1), (b0, b1) in zip(ch, ch[1:]):
+            assert a1 == b0 and (a1 - a0) % D.TILE == 0 and a1 - a0 >= 1024

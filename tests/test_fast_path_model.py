@@ -37,12 +37,26 @@ def test_scan_restatement_matches_oracle():
     assert np.array_equal(scan_np(v), np.array([O.e2m1_code(float(x)) for x in v], dtype=np.uint8))
 
 
+TINY = np.float32(2.0 ** -149)
+
+
 def stand_in_bits(v: np.ndarray) -> np.ndarray:
-    """The GPU quantizer's stand-in for v = RN(x * inv): -0 folded to +0 (the
-    product is formed as fma(x, inv, +0)), then (max(b, 1) - 1) | 1 on the bits."""
-    b = v.astype(np.float32).view(np.uint32).copy()
-    b[b == np.uint32(0x80000000)] = 0
-    return ((np.maximum(b, np.uint32(1)) - np.uint32(1)) | np.uint32(1)).astype(np.uint32)
+    """The GPU quantizer's stand-in for an already rounded v = RN(x * inv):
+    v' = RN(v + 2^-149) (the kernel forms RN(x * inv + 2^-149) in one fma; for a
+    v that is not a zero nor within 2^-142 of one, adding 2^-149 to v or to the
+    exact product rounds alike except at exact midpoints, which
+    test_denormal_addend_changes_no_code covers), then (b - 1) | 1 on the bits."""
+    with np.errstate(over="ignore"):
+        vp = (v.astype(np.float32) + TINY).astype(np.float32)
+    b = vp.view(np.uint32).copy()
+    return ((b - np.uint32(1)) | np.uint32(1)).astype(np.uint32)
+
+
+def reachable(pats: np.ndarray) -> np.ndarray:
+    """Scaled values the fast path can produce: zeros and |v| >= 2^-142 (a BF16
+    x is 0 or at least 2^-133 in magnitude, 1 / scale at least 1/480)."""
+    mag = pats & np.uint32(0x7FFFFFFF)
+    return pats[(mag == 0) | (mag >= np.float32(2.0 ** -142).view(np.uint32))]
 
 
 def e2m1_rne_np(bits: np.ndarray) -> np.ndarray:
@@ -68,7 +82,7 @@ def test_hardware_rounding_of_stand_in_equals_scan():
                            rng.integers(0, int(limit), 1_000_000, dtype=np.uint32),
                            np.array([0, 1, 2, 3, 0x00800000, 0x007FFFFF, 0x4AFFFFFF], dtype=np.uint32)])
     pats = pats[pats < limit]
-    pats = np.concatenate([pats, pats | np.uint32(0x80000000)])
+    pats = reachable(np.concatenate([pats, pats | np.uint32(0x80000000)]))
     v = pats.view(np.float32)
     assert np.array_equal(e2m1_rne_np(stand_in_bits(v)), scan_np(v))
 
@@ -78,6 +92,7 @@ def test_stand_in_special_values():
     # the halfway values go to the lower magnitude (0.75 -> 0.5, 1.75 -> 1.5, 3.5 -> 3).
     v = np.array([0.0, -0.0, 1e-30, -1e-30, -2.0 ** -140, 0.75, -0.75, 1.75, 3.5, -3.5, 5.0, 0.25, 1.25, 2.5,
                   6.0, 7.0, 1e6], dtype=np.float32)
+    assert len(reachable(v.view(np.uint32))) == len(v)
     got = e2m1_rne_np(stand_in_bits(v))
     assert got.tolist() == [0, 0, 0, 8, 8, 1, 9, 3, 5, 13, 6, 0, 2, 4, 7, 7, 7]
     assert np.array_equal(got, scan_np(v))
@@ -124,3 +139,44 @@ def test_scale_table_matches_oracle_for_every_fast_path_absmax():
     got = np.array([sf[O.sf_index(r, 0, 8)] for r in range(len(bits))], dtype=np.uint8)
     assert np.all(got[:0x3C40] == 0x01)
     assert np.array_equal(got[0x3C40:], table)
+
+
+def ue4m3_value(b: int) -> float:
+    e, m = (b >> 3) & 0xF, b & 7
+    return m * 2.0 ** -9 if e == 0 else (8 + m) * 2.0 ** (e - 10)
+
+
+def test_denormal_addend_changes_no_code():
+    # The kernel scales with fma(x, inv, 2^-149) instead of x * inv.  For every
+    # fast-path BF16 x (finite, |x| < 2^30, non-zero) and every reciprocal
+    # inv = RN(1 / ue4m3(s)), the product x * inv is exact in float64; where it
+    # is exactly halfway between two floats, RN(x * inv) picks the even one
+    # while the addend pushes positive products to the larger and negative
+    # ones to the smaller magnitude.  Both must have the same reference code.
+    mids = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0])
+
+    def code(v):
+        return np.searchsorted(mids, np.abs(v), side="left") + np.where(v < 0, 8, 0)
+
+    bits = np.arange(65536, dtype=np.uint32)
+    with np.errstate(invalid="ignore"):
+        x = (bits << 16).view(np.float32).astype(np.float64)
+    x = x[np.isfinite(x) & (np.abs(x) < 2.0 ** 30) & (x != 0)]
+    assert np.abs(x).min() * (1.0 / 480.0) >= 2.0 ** -142
+    halfway = 0
+    for s in range(1, 128):
+        inv = np.float64(np.float32(1.0) / np.float32(ue4m3_value(s)))
+        p = x * inv
+        b = p.view(np.uint64)
+        normal = ((b >> np.uint64(52)) & np.uint64(0x7FF)).astype(np.int64) - 1023 >= -126
+        mid = normal & ((b & np.uint64((1 << 29) - 1)) == np.uint64(1 << 28))
+        if not mid.any():
+            continue
+        pm = p[mid]
+        below = (pm.view(np.uint64) & ~np.uint64((1 << 29) - 1)).view(np.float64)  # toward zero
+        above = below + 2 * (pm - below)                                         # away from zero
+        with_addend = np.where(pm > 0, above, below)
+        rne = pm.astype(np.float32).astype(np.float64)
+        assert np.array_equal(code(rne), code(with_addend)), f"scale byte {s}"
+        halfway += int(mid.sum())
+    assert halfway > 0  # the case does occur

@@ -211,26 +211,28 @@ def test_forward_host_equals_forward(cuda, fp4, m, chunk):
                                       (512, 2880, 2880, "128"), (512, 2880, 2880, "192"), (512, 2880, 2880, "256"),
                                       (512, 2880, 2880, "320"), (512, 2880, 2880, "384"),
                                       (4096, 2880, 2880, None)])
-def test_fused_quantize_gemm_equals_two_kernels(cuda, fp4, monkeypatch, m, n, k, bn):
-    # With FP4B_FUSE=1 and M > 128 the cached linear quantizes the activations
-    # inside the GEMM kernel when its tiles fit in one round of CTA pairs (the
-    # last shape does not: two kernels run); the result must be the
-    # two-kernel path's bytes exactly, for every tile width, ragged M and K,
-    # a K that ends half-way through a 256-wide stage, and repeated launches.
+def test_overlapped_quantize_gemm_equals_two_kernels(cuda, fp4, monkeypatch, m, n, k, bn):
+    # With FP4B_OVERLAP=1 a cached linear whose tiles fit in one round of CTA
+    # pairs runs the activation quantizer and the GEMM side by side (the GEMM
+    # waits for the units of A it needs); the last shape needs two rounds and
+    # runs the two kernels in turn.  The bytes must be the two-kernel path's exactly
+    # (FP4B_OVERLAP=0), for every tile width, ragged M and K, a K that ends
+    # half-way through a 256-wide stage, and repeated launches (the unit
+    # counters are reused).
     if bn:
         monkeypatch.setenv("FP4B_FORCE_BN", bn)
     x, w, b = W.cached_linear_inputs(m, n, k, seed=23)
     with fp4.FP4WeightCache(w.to(cuda), b.to(cuda)) as cache:
         xd = x.to(cuda)
-        monkeypatch.setenv("FP4B_FUSE", "0")
+        monkeypatch.setenv("FP4B_OVERLAP", "0")
         two = cache.forward(xd)
-        monkeypatch.setenv("FP4B_FUSE", "1")
-        fused = [cache.forward(xd) for _ in range(3)]  # repeated launches reuse the tile counters
+        monkeypatch.setenv("FP4B_OVERLAP", "1")
+        overlapped = [cache.forward(xd) for _ in range(3)]
         torch.cuda.synchronize()
-        for f in fused:
+        for f in overlapped:
             assert torch.equal(f, two)
         assert fp4.device_error() == 0
-    assert_gemm_close(two, oracle_linear(x, w, bias=b), f"fused {m}x{n}x{k}")
+    assert_gemm_close(two, oracle_linear(x, w, bias=b), f"overlapped {m}x{n}x{k}")
 
 
 @pytest.mark.parametrize("m,n,k,bn", [(2048, 2880, 7680, None), (4096, 5760, 2880, "256"), (384, 1000, 640, "128"),

@@ -52,7 +52,15 @@ def _worker(rank, world, port, q):
         assert torch.equal(tp.forward(xd), ref)  # first buffer again
         nc = D.ColumnParallelFP4Linear(wd, bd, mode="nccl")
         assert torch.equal(nc.forward(xd), ref)
-        small = tp.forward(xd[:100])  # M <= 128 takes the all-gather path
+        ep = D.ColumnParallelFP4Linear(wd, bd, mode="epilogue")  # the GEMM epilogue stores to the peers
+        assert ep.uses_p2p(m)
+        assert torch.equal(ep.forward(xd[:256]), single.forward(xd[:256]))
+        assert torch.equal(ep.forward(xd), ref)
+        assert torch.equal(ep.forward(xd[:100]), single.forward(xd[:100]))  # M <= 128: all-gather
+        ep.free()
+        big = W.normal_bf16((2304, k), 1.0, 5).to(dev)  # several copy-engine row chunks (1024-row minimum)
+        assert torch.equal(tp.forward(big), single.forward(big))
+        small = tp.forward(xd[:100])  # copy-engine mode at M <= 128 too
         assert torch.equal(small, single.forward(xd[:100]))
         nc.free()
         r0, r1 = D.row_range(m, world, rank)
