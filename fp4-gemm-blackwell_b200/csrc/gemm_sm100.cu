@@ -128,9 +128,11 @@ struct Params {
 };
 
 // Output tensor maps of the peer buffers (column-parallel mode); all zero and
-// unused otherwise.
+// unused otherwise.  map: 32 x 32 boxes (the last tile's chunks); map64:
+// 16 x 64 boxes (every other tile's pieces).
 struct PeerMaps {
     CUtensorMap map[kMaxPeers];
+    CUtensorMap map64[kMaxPeers];
 };
 
 // Tile t -> (row tile, column tile) in groups of kTileGroupRows rows of A: the
@@ -298,6 +300,41 @@ __device__ __forceinline__ void store_staged_chunk(const Params& p, const CUtens
     if (lane == (chunk_iter & 31)) {
         ptx::tma_store_2d(tmap_d, buf, n, row0);
         for (int d = 0; d < p.npeers; ++d) ptx::tma_store_2d(&pm->map[d], buf, n, row0);
+        ptx::bulk_commit_group();
+    }
+}
+
+// Stores a 16 x 64 piece of the output: rows [row0, row0 + 16) (held by lanes
+// 16 half .. 16 half + 15) of two adjacent converted 32-column chunks (lo:
+// columns [n, n + 32), hi: [n + 32, n + 64)).  The rows go into the warp's
+// 2 KB buffer in the TMA 128-byte swizzle (16-byte unit u of row r at unit
+// u ^ (r & 7): 8 consecutive rows on distinct banks), then one lane stores
+// the box locally and into every peer's buffer.  A piece has 128-byte rows:
+// SM-issued stores into another GPU's memory reach ~640 GB/s in each
+// direction at once with rows of 128 bytes or more, ~430 GB/s with the
+// 64-byte rows of a 32 x 32 chunk (measured on B200, two GPUs).  Same
+// rotating-lane protocol as store_staged_chunk.
+__device__ __forceinline__ void store_piece(const Params& p, const CUtensorMap* tmap_d64, const PeerMaps* pm,
+                                            const uint32_t (&lo)[16], const uint32_t (&hi)[16], uint8_t* buf,
+                                            int row0, int n, int half, int lane, int chunk_iter) {
+    if (lane == ((chunk_iter - 1) & 31)) ptx::bulk_wait_group_read<0>();
+    __syncwarp();
+    const unsigned r = (unsigned)(lane - 16 * half);
+    if (r < 16u) {
+        // Row r starts 128-byte aligned, so unit u ^ (r & 7) of it is at
+        // (row + 16 (r & 7)) ^ 16 u: one base register, an XOR per store.
+        const uint32_t a = ptx::smem_u32(buf) + 128u * r + 16u * (r & 7u);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            ptx::st_shared_v4(a ^ (16u * u), lo[4 * u], lo[4 * u + 1], lo[4 * u + 2], lo[4 * u + 3]);
+            ptx::st_shared_v4(a ^ (16u * (u + 4)), hi[4 * u], hi[4 * u + 1], hi[4 * u + 2], hi[4 * u + 3]);
+        }
+    }
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == (chunk_iter & 31)) {
+        ptx::tma_store_2d(tmap_d64, buf, n, row0);
+        for (int d = 0; d < p.npeers; ++d) ptx::tma_store_2d(&pm->map64[d], buf, n, row0);
         ptx::bulk_commit_group();
     }
 }
@@ -581,7 +618,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ([row tile][k-block][512 bytes]) so they too can complete on CTA 0's barrier.
 //
 // 416 threads: warps 0-7 epilogue (warp w reads TMEM lanes 32(w%4)..+31 and
-// stores the 32-column chunks c with c % 2 == w / 4), warp 8 TMEM allocation
+// stores the 64-column super-chunks s with s % 2 == w / 4 as 16 x 64 pieces;
+// with an odd count the last super-chunk is split by rows: warp w stores its
+// rows 16 (w / 4) .. +15), warp 8 TMEM allocation
 // and MMA issue, warps 9-12 one producer per copy type
 // (A, B, scale-A, scale-B).  The pair's last tile is stored by all 13 warps
 // (team_epilogue): the MMA and producer warps have nothing left to do.  A TMA issue keeps its warp busy for ~130 ns on
@@ -616,9 +655,10 @@ struct PairCfg {
     // always brings the same bytes: those of both CTAs land on CTA 0's barrier.
     static constexpr uint32_t TX_BYTES = 2u * STAGE_BYTES;
     static constexpr int BAR_BYTES = 256;
-    // Epilogue staging: one 32 x 32 BF16 buffer (2 KB) and half the tile's bias per epilogue warp.
-    static constexpr int EPI_BYTES = kPairEpiWarps * 2048;          // one 32 x 32 BF16 buffer per epilogue warp
-    static constexpr int BIAS_BYTES = kPairEpiWarps * (TW / 2) * 2;  // BF16 bias of each warp's half of the tile
+    // Epilogue staging: one 2 KB BF16 buffer (a 16 x 64 piece or a 32 x 32
+    // chunk) and the tile's BF16 bias per epilogue warp.
+    static constexpr int EPI_BYTES = kPairEpiWarps * 2048;
+    static constexpr int BIAS_BYTES = kPairEpiWarps * TW * 2;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + BIAS_BYTES + BAR_BYTES + 1024;
     static constexpr int SF_COLS = 4 * kKbPerStage * (1 + NRT);
     static constexpr int ACC_BUFS = (2 * TW + SF_COLS <= (int)kTmemCols) ? 2 : 1;
@@ -649,8 +689,8 @@ constexpr int kPairFirstProducer = 9;
 // quadrant q: the two epilogue warps q and q + 4 (members 0, 1) and the warps
 // whose roles have ended (8 and 12 on quadrant 0, 9, 10, 11 on quadrants 1-3).
 // Member ti of ts takes 32-column chunks c = ti, ti + ts, ...
-// Chunk c's BF16 bias was staged by epilogue warp q + 4 (c & 1) at uint4
-// offset 4 (c >> 1).  tq: TMEM address of the quadrant's accumulator; ring:
+// The tile's BF16 bias was staged by epilogue warp q (chunk c at uint4
+// offset 4 c).  tq: TMEM address of the quadrant's accumulator; ring:
 // the operand ring, idle once the last tile's MMAs have completed, in which
 // chunk c of quadrant q is staged in a 2 KB slot of its own (q * CH + c), so no
 // chunk waits for an earlier TMA store to finish reading its buffer; m: this
@@ -669,7 +709,7 @@ __device__ __forceinline__ void team_epilogue(const Params& p, const CUtensorMap
         if (n0 + 32 * c >= p.n_out) continue;
         if (p.tma_store) {
             uint32_t pk[16];
-            convert_chunk(p, r, sBias + (q + 4 * (c & 1)) * (TW / 16) + 4 * (c >> 1), pk);
+            convert_chunk(p, r, sBias + q * (TW / 8) + 4 * c, pk);
             if (m - lane < p.m)  // the warp's 32 rows start inside D
                 store_staged_chunk(p, tmap_d, pm, pk, ring + (size_t)(q * CH + c) * 2048, m - lane, n0 + 32 * c,
                                    lane, chunk_iter++, true);
@@ -684,8 +724,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     nvf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_b1,
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-                          const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ Params p,
-                          const __grid_constant__ PeerMaps pm) {
+                          const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ CUtensorMap tmap_d64,
+                          const __grid_constant__ Params p, const __grid_constant__ PeerMaps pm) {
     using C = PairCfg<BN, STAGES, NSUB, BN1>;
     constexpr int TW = C::TW;
     constexpr int TILE_M = 2 * kBM;
@@ -733,7 +773,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         if (NSUB > 1) ptx::prefetch_tmap(&tmap_b1);
         ptx::prefetch_tmap(&tmap_sfa);
         ptx::prefetch_tmap(&tmap_sfb);
-        if (p.tma_store) ptx::prefetch_tmap(&tmap_d);
+        if (p.tma_store) {
+            ptx::prefetch_tmap(&tmap_d);
+            ptx::prefetch_tmap(&tmap_d64);
+        }
     }
     if (warp == kPairMmaWarp) {
         ptx::tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -928,11 +971,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     } else {
         // ------------------------------------------------------------ epilogue (both CTAs)
         const int q = warp & 3;   // TMEM lane quadrant
-        const int h = warp >> 2;  // chunks c = h, h + 2, ...
-        constexpr int kMyChunks = TW / 64;
+        const int h = warp >> 2;  // super-chunks s = h, h + 2, ...
+        constexpr int S = TW / 64;                      // 64-column super-chunks of a tile
+        constexpr int kFull = S / 2;                    // whole super-chunks per warp
+        constexpr bool kSplit = (S & 1) != 0;           // the last one is split by rows between the two warps
+        constexpr int kIters = kFull + (kSplit ? 1 : 0);
         const uint32_t acc_empty0 = ptx::map_to_cta(ptx::smem_u32(acc_empty), 0);
         uint8_t* epi = sEpi + warp * 2048;
-        uint4* wbias = sBias + warp * (TW / 16);
+        uint4* wbias = sBias + warp * (TW / 8);
         int chunk_iter = 0;
         int tile_iter = 0;
         for (int t = pair; t < p.num_tiles; t += npairs, ++tile_iter) {
@@ -945,7 +991,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             if (p.bias) {
                 __syncwarp();  // the previous tile's reads of wbias are done
 #pragma unroll
-                for (int j = 0; j < kMyChunks; ++j) stage_bias(p, wbias + 4 * j, n0 + 32 * (h + 2 * j), 32, lane);
+                for (int c = 0; c < TW / 32; ++c) stage_bias(p, wbias + 4 * c, n0 + 32 * c, 32, lane);
                 __syncwarp();
             }
             if (last_tile && lane == 0) ptx::mbar_arrive(bias_ready);
@@ -973,46 +1019,61 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             }
             // Only a later tile of this pair that reuses accumulator b waits for it.
             const bool release = t + C::ACC_BUFS * npairs < p.num_tiles;
-            // Chunks go two at a time: both are converted together (independent
-            // work for the warp's latency), then the next two TMEM loads are issued
-            // into the freed registers while the converted pair is stored.
-            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + b * TW + 32 * h;
+            // One super-chunk (two 32-column TMEM loads) per iteration: both halves
+            // are converted together (independent work for the warp's latency), then
+            // the next super-chunk's loads are issued into the freed registers while
+            // the converted one is stored.
+            const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + b * TW;
+            const int row0 = m - lane;  // the warp's first row
+            const uint4* wbh = wbias + 8 * h;
             uint32_t ra[32], rb[32];
-            ptx::tmem_ld_32x32b_x32(tbase, ra);
-            if (kMyChunks > 1) ptx::tmem_ld_32x32b_x32(tbase + 64, rb);
+            ptx::tmem_ld_32x32b_x32(tacc + 64 * h, ra);
+            ptx::tmem_ld_32x32b_x32(tacc + 64 * h + 32, rb);
 #pragma unroll
-            for (int j = 0; j < kMyChunks; j += 2) {
-                const bool two = j + 1 < kMyChunks;
-                const int c0 = h + 2 * j, c1 = c0 + 2;
-                const bool in0 = n0 + 32 * c0 < p.n_out, in1 = two && n0 + 32 * c1 < p.n_out;
+            for (int j = 0; j < kIters; ++j) {
+                const bool split = kSplit && j == kFull;
+                const int sc = split ? S - 1 : h + 2 * j;
+                const int nsc = (j + 1 == kFull && kSplit) ? S - 1 : h + 2 * (j + 1);  // next iteration's
+                const int nc = n0 + 64 * sc;
                 ptx::tmem_ld_wait();
                 if (p.tma_store) {
                     uint32_t pa[16], pb[16];
-                    convert_chunk(p, ra, wbias + 4 * j, pa);
-                    if (two) convert_chunk(p, rb, wbias + 4 * (j + 1), pb);
-                    if (j + 2 < kMyChunks) {
-                        ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 2), ra);
-                        if (j + 3 < kMyChunks) ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 3), rb);
+                    const uint4* bsc = (kSplit && split) ? wbias + 8 * (S - 1) : wbh + 16 * j;  // chunks 2 sc, 2 sc + 1
+                    convert_chunk(p, ra, bsc, pa);
+                    convert_chunk(p, rb, bsc + 4, pb);
+                    if (j + 1 < kIters) {
+                        ptx::tmem_ld_32x32b_x32(tacc + 64 * nsc, ra);
+                        ptx::tmem_ld_32x32b_x32(tacc + 64 * nsc + 32, rb);
                     } else if (release) {
                         // Every TMEM read of this accumulator is done: hand it back to the MMA issuer.
                         ptx::tc_fence_before();
                         __syncwarp();
                         if (lane == 0) ptx::mbar_arrive_cluster(acc_empty0 + (uint32_t)b * 8u);
                     }
-                    if (m - lane < p.m) {  // the warp's 32 rows start inside D
-                        if (in0)
-                            store_staged_chunk(p, &tmap_d, &pm, pa, epi, m - lane, n0 + 32 * c0, lane, chunk_iter++);
-                        if (in1)
-                            store_staged_chunk(p, &tmap_d, &pm, pb, epi, m - lane, n0 + 32 * c1, lane, chunk_iter++);
+                    if (nc < p.n_out) {
+                        if (!split) {
+                            if (row0 < p.m)
+                                store_piece(p, &tmap_d64, &pm, pa, pb, epi, row0, nc, 0, lane, chunk_iter++);
+                            if (row0 + 16 < p.m)
+                                store_piece(p, &tmap_d64, &pm, pa, pb, epi, row0 + 16, nc, 1, lane, chunk_iter++);
+                        } else if (row0 + 16 * h < p.m) {
+                            store_piece(p, &tmap_d64, &pm, pa, pb, epi, row0 + 16 * h, nc, h, lane, chunk_iter++);
+                        }
                     }
                 } else {
                     if (m < p.m) {
-                        if (in0) store_chunk(p, ra, m, n0 + 32 * c0);
-                        if (in1) store_chunk(p, rb, m, n0 + 32 * c1);
+                        if (!split) {
+                            if (nc < p.n_out) store_chunk(p, ra, m, nc);
+                            if (nc + 32 < p.n_out) store_chunk(p, rb, m, nc + 32);
+                        } else if (h == 0) {
+                            if (nc < p.n_out) store_chunk(p, ra, m, nc);
+                        } else if (nc + 32 < p.n_out) {
+                            store_chunk(p, rb, m, nc + 32);
+                        }
                     }
-                    if (j + 2 < kMyChunks) {
-                        ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 2), ra);
-                        if (j + 3 < kMyChunks) ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 3), rb);
+                    if (j + 1 < kIters) {
+                        ptx::tmem_ld_32x32b_x32(tacc + 64 * nsc, ra);
+                        ptx::tmem_ld_32x32b_x32(tacc + 64 * nsc + 32, rb);
                     } else if (release) {
                         ptx::tc_fence_before();
                         __syncwarp();
@@ -1160,16 +1221,17 @@ bool make_scale_map(CUtensorMap* map, const void* base, long rows_pad, long k_pa
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// BF16 output D [m, n_out] with row stride ldd, 32 x 32 boxes, 64-byte swizzle.
-bool make_output_map(CUtensorMap* map, void* base, long m, long n_out, long ldd) {
+// BF16 output D [m, n_out] with row stride ldd: 32 x 32 boxes with the 64-byte
+// swizzle, or (wide) 16-row x 64-column boxes with the 128-byte swizzle.
+bool make_output_map(CUtensorMap* map, void* base, long m, long n_out, long ldd, bool wide) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)n_out, (cuuint64_t)m};
     const cuuint64_t strides[1] = {(cuuint64_t)(ldd * 2)};
-    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t box[2] = {wide ? 64u : 32u, wide ? 16u : 32u};
     const cuuint32_t estr[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               wide ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -1238,7 +1300,7 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const Q
     std::call_once(attr_once[dev & 63], [&] {
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     });
-    CUtensorMap ma, mb, mb1, msa, msb, md;
+    CUtensorMap ma, mb, mb1, msa, msb, md, md64;
     if (!make_operand_map(&ma, g.a_fp4, g.m_rows_pad, g.k_pad, kBM) ||
         !make_operand_map(&mb, g.b_fp4, g.n_rows_pad, g.k_pad, C::BH) ||
         !make_operand_map(&mb1, g.b_fp4, g.n_rows_pad, g.k_pad, C::BH1) ||
@@ -1248,15 +1310,20 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const Q
     Params p = make_params(g, C::TW, 2 * kBM);
     // D through TMA stores when C is not read and D's rows are 16-byte aligned.
     memset(&md, 0, sizeof(md));
+    memset(&md64, 0, sizeof(md64));
     const bool no_c = !g.c || g.beta == 0.0f;
     const bool d_ok = (reinterpret_cast<uintptr_t>(g.d) & 15) == 0 && g.ldd % 8 == 0;
-    if (no_c && d_ok && make_output_map(&md, g.d, g.m, g.n_out, g.ldd)) p.tma_store = 1;
+    if (no_c && d_ok && make_output_map(&md, g.d, g.m, g.n_out, g.ldd, false) &&
+        make_output_map(&md64, g.d, g.m, g.n_out, g.ldd, true))
+        p.tma_store = 1;
     PeerMaps pm;
     memset(&pm, 0, sizeof(pm));
     if (npeers > 0) {
         if (!p.tma_store || npeers > kMaxPeers) return cudaErrorNotSupported;
         for (int i = 0; i < npeers; ++i)
-            if (!make_output_map(&pm.map[i], peers[i], g.m, g.n_out, g.ldd)) return cudaErrorNotSupported;
+            if (!make_output_map(&pm.map[i], peers[i], g.m, g.n_out, g.ldd, false) ||
+                !make_output_map(&pm.map64[i], peers[i], g.m, g.n_out, g.ldd, true))
+                return cudaErrorNotSupported;
         p.npeers = npeers;
     }
     const int pairs = max_pairs(kernel, C::SMEM_BYTES, sms, kPairThreads);
@@ -1276,13 +1343,13 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const Q
         const cudaError_t e = quantize_units_launch(*qa, ready, ring, sms, stream);
         if (e != cudaSuccess) return e;
         const cudaError_t e2 = launch_dependent(kernel, dim3(grid), dim3(kPairThreads), C::SMEM_BYTES, stream, ma,
-                                                mb, mb1, msa, msb, md, p, pm);
+                                                mb, mb1, msa, msb, md, md64, p, pm);
         if (e2 != cudaSuccess)  // the quantizer ran alone: leave the counters zero for the next launch
             cudaMemsetAsync(ready, 0, (size_t)(p.ready_count + 1) * sizeof(uint32_t), stream);
         return e2;
     }
     return launch_dependent(kernel, dim3(grid), dim3(kPairThreads), C::SMEM_BYTES, stream, ma, mb, mb1, msa, msb, md,
-                            p, pm);
+                            md64, p, pm);
 }
 
 template <int BN, int STAGES, int CHUNKS>

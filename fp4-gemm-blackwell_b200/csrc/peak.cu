@@ -10,7 +10,8 @@
 // the GEMM's roofline is measured against.  The other arguments reproduce the
 // GEMM mainloop's tensor-pipe work per k-block without its loads: two MMAs of
 // widths n0 and n1 on the same A tile (the 320- and 384-wide tiles) and the
-// tcgen05.cp copies of the scale atoms (one for A plus `sfb_atoms` for B).
+// tcgen05.cp copies of the scale atoms (one for A plus `sfb_atoms` for B),
+// issued like the GEMM issues them: each k-block's copies right before its MMAs.
 // The final wait is bounded; the stage count is capped so that a launch runs
 // for well under a second.
 #include <cuda_runtime.h>
@@ -87,28 +88,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kRateThreads, 1)
         const uint32_t sfa_t = tmem + kTmemSfa, sfb_t = tmem + kTmemSfb;
         for (int it = 0; it < stages; ++it) {
             if (ptx::elect_one()) {
-                if (it == 0) {
-                    // Every scale column the MMAs read holds a valid scale from the start.
+                // Like the GEMM: each k-block's scale copies right before its MMAs.
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
+                for (int j = 0; j < 4; ++j) {
+                    if (it == 0 || sf_copies) {
                         ptx::tc_cp_32x128b_warpx4_pair(sfa_t + 4 * j, sfadesc + (uint64_t)((j * kAtom) >> 4));
 #pragma unroll
                         for (int r = 0; r < kMaxSfbAtoms; ++r)
-                            ptx::tc_cp_32x128b_warpx4_pair(sfb_t + j * 4 * kMaxSfbAtoms + 4 * r,
-                                                           sfbdesc + (uint64_t)(((r * 4 + j) * kAtom) >> 4));
+                            if (it == 0 || r < SFB)  // the first stage fills every scale column the MMAs read
+                                ptx::tc_cp_32x128b_warpx4_pair(sfb_t + j * 4 * kMaxSfbAtoms + 4 * r,
+                                                               sfbdesc + (uint64_t)(((r * 4 + j) * kAtom) >> 4));
                     }
-                } else if (sf_copies) {
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        ptx::tc_cp_32x128b_warpx4_pair(sfa_t + 4 * j, sfadesc + (uint64_t)((j * kAtom) >> 4));
-#pragma unroll
-                        for (int r = 0; r < SFB; ++r)
-                            ptx::tc_cp_32x128b_warpx4_pair(sfb_t + j * 4 * kMaxSfbAtoms + 4 * r,
-                                                           sfbdesc + (uint64_t)(((r * 4 + j) * kAtom) >> 4));
-                    }
-                }
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
                     const uint32_t koff = (uint32_t)((32 * j) >> 4);
                     const uint32_t acc_flag = (it | j) ? 1u : 0u;
                     ptx::tc_mma_nvf4_pair(tmem, adesc + koff, bdesc + koff, idesc0, sfa_t + 4 * j,

@@ -11,18 +11,20 @@ single-GPU kernels of ``fp4_gemm``:
   and keeps only its 128-row slice of W (the same bytes as that slice of the
   full cache, because quantization is row-local and scale atoms cover 128
   rows).  Each rank computes its output columns and the result is assembled
-  as [M, N] on every rank, in one of three ways:
-    - "p2p" (the default): every rank's [M, N] buffer is mapped by every other
-      rank (CUDA IPC).  The rank's GEMM writes its columns into its own
-      buffer in row chunks, and a side stream pushes each finished chunk to
-      every peer's buffer with a strided copy-engine copy over NVLink while
-      the next chunk is computed; a flag barrier on the GPU
-      (``PeerFlagBarrier``: one warp signals every peer and waits for every
-      peer's signal) then orders the ranks.  No gather buffer, no re-layout,
-      no collective, and the GEMM runs at its single-GPU speed.
-    - "epilogue": the GEMM epilogue itself stores every output tile into all
-      ranks' buffers (TMA bulk stores over NVLink), then the flag barrier.
+  as [M, N] on every rank in one of these modes:
+    - "epilogue": every rank's [M, N] buffer is mapped by every other rank
+      (CUDA IPC), and the GEMM epilogue stores every output piece into all
+      ranks' buffers (TMA bulk stores of 16 x 64 pieces: 128-byte rows, which
+      SM stores over NVLink need for full rate), so the transfer overlaps
+      the GEMM tile by tile; a flag barrier on the GPU (``PeerFlagBarrier``:
+      one warp signals every peer and waits for every peer's signal) then
+      orders the ranks.  No gather buffer, no re-layout, no collective.
       Needs M > 128 (the CTA-pair kernel) and N a multiple of 8.
+    - "p2p": the same mapped buffers, but the GEMM writes only this rank's
+      buffer, in row chunks, and a side stream pushes each finished chunk to
+      every peer with a strided copy-engine copy while the next chunk is
+      computed; then the flag barrier.  Any M.
+    - "auto" (the default): "epilogue" where it applies, else "p2p".
     - "nccl": one NCCL all-gather of equal-size, zero-padded slices and a
       re-layout.
 
@@ -197,8 +199,8 @@ class ColumnParallelFP4Linear:
     """N-sharded weight cache; the output columns of all ranks are assembled.
 
     `weight` is the full [N, K] BF16 weight (each rank slices its own rows);
-    the output of ``forward`` is the full [M, N] on every rank.  With
-    mode "p2p" (the default where it applies) the result is a view of one of
+    the output of ``forward`` is the full [M, N] on every rank.  In the
+    mapped-buffer modes ("auto", "epilogue", "p2p") it is a view of one of
     two per-layer buffers that the ranks write into each other: work queued
     before this rank's next ``forward`` of the layer may read it (the peers
     write the same buffer again in the forward after that, once this rank
@@ -235,6 +237,12 @@ class ColumnParallelFP4Linear:
         if self.mode == "epilogue":
             return m > 128 and self.n % 8 == 0
         return True
+
+    def _epilogue(self, m: int) -> bool:
+        """Whether a mapped-buffer forward of M rows has the GEMM epilogue store the
+        peers' copies ("epilogue", and "auto" where the CTA-pair kernel runs)
+        rather than the copy engine ("p2p")."""
+        return self.mode == "epilogue" or (self.mode == "auto" and m > 128 and self.n % 8 == 0)
 
     def _ensure_buffers(self, m: int):
         import fp4_gemm
@@ -285,7 +293,7 @@ class ColumnParallelFP4Linear:
         out = self._bufs[self._flip, :m]
         sh = self.shards[self.rank]
         bases = {q: b for q, (b, _) in self._peer_bases.items()}
-        if self.mode == "epilogue":
+        if self._epilogue(m):
             if sh.cols > 0:
                 peers = peer_targets(bases, self.rank, self.world, self._flip, cap, self.n, sh.start)
                 fp4_gemm.run_cached_peers(x2, self.cache, out[:, sh.start:sh.stop], peers)

@@ -43,10 +43,10 @@ def _worker(rank, world, port, q):
         y = tp.forward(xd)
         ref = single.forward(xd)
         assert_gemm_close(y, ref.float(), f"column-parallel rank {rank}")
-        # Column tiles of a shard run the same MMAs as in the full GEMM: both
-        # assembly modes give the single-GPU bytes exactly.
-        assert tp.uses_p2p(m)
-        assert torch.equal(y, ref), "p2p column-parallel differs from one GPU"
+        # Column tiles of a shard run the same MMAs as in the full GEMM: every
+        # assembly mode gives the single-GPU bytes exactly.
+        assert tp.uses_p2p(m) and tp._epilogue(m)  # "auto": the epilogue stores to the peers
+        assert torch.equal(y, ref), "column-parallel differs from one GPU"
         y2 = tp.forward(xd[:384])  # second buffer, fewer rows
         assert torch.equal(y2, single.forward(xd[:384]))
         assert torch.equal(tp.forward(xd), ref)  # first buffer again
@@ -58,10 +58,17 @@ def _worker(rank, world, port, q):
         assert torch.equal(ep.forward(xd), ref)
         assert torch.equal(ep.forward(xd[:100]), single.forward(xd[:100]))  # M <= 128: all-gather
         ep.free()
+        ce = D.ColumnParallelFP4Linear(wd, bd, mode="p2p")  # copy-engine pushes
+        assert ce.uses_p2p(m) and not ce._epilogue(m)
+        assert torch.equal(ce.forward(xd), ref)
         big = W.normal_bf16((2304, k), 1.0, 5).to(dev)  # several copy-engine row chunks (1024-row minimum)
-        assert torch.equal(tp.forward(big), single.forward(big))
-        small = tp.forward(xd[:100])  # copy-engine mode at M <= 128 too
+        want_big = single.forward(big)
+        assert torch.equal(ce.forward(big), want_big)
+        assert torch.equal(tp.forward(big), want_big)  # auto: epilogue stores, several tiles per CTA pair
+        small = tp.forward(xd[:100])  # auto at M <= 128: copy-engine pushes
+        assert not tp._epilogue(100)
         assert torch.equal(small, single.forward(xd[:100]))
+        ce.free()
         nc.free()
         r0, r1 = D.row_range(m, world, rank)
         dp = D.DataParallelFP4Linear(wd, bd)

@@ -20,11 +20,15 @@ SENTINEL = -12288.0  # exact in BF16, never produced by these inputs
 GUARD = 4096
 
 
-@pytest.mark.parametrize("pair,bn,m", [(0, 128, 100), (0, 256, 128), (1, 192, 300), (1, 256, 300), (1, 320, 300),
-                                       (1, 384, 300), (1, 128, 4096), (1, 384, 8192)])
+@pytest.mark.parametrize("pair,bn,m,n", [(0, 128, 100, 1000), (0, 256, 128, 1000), (1, 192, 300, 1000),
+                                         (1, 256, 300, 1000), (1, 320, 300, 1000), (1, 384, 300, 1000),
+                                         (1, 128, 4096, 1000), (1, 384, 8192, 1000),
+                                         # more column tiles than CTA pairs: the ragged last row tile is
+                                         # stored by the per-tile epilogue too, not only the last-tile team
+                                         (1, 128, 300, 10000), (1, 192, 300, 14500), (1, 320, 300, 24000)])
 @pytest.mark.parametrize("ldd_extra", [24, 3])
-def test_gemm_writes_only_its_output(cuda, fp4, monkeypatch, pair, bn, m, ldd_extra):
-    n, k = 1000, 640
+def test_gemm_writes_only_its_output(cuda, fp4, monkeypatch, pair, bn, m, n, ldd_extra):
+    k = 640
     monkeypatch.setenv("FP4B_PAIR", str(pair))
     monkeypatch.setenv("FP4B_FORCE_BN", str(bn))
     x, w, b = W.cached_linear_inputs(m, n, k, seed=61)
