@@ -376,10 +376,9 @@ FP4B_EXPORT int fp4b_run_cached_ex(const void* A, int m, int k_in, int lda, cons
 FP4B_EXPORT int fp4b_run_cached_peers(const void* A, int m, int k_in, int lda, const void* h, int n_out,
                                       void* D, int ldd, void* const* peer_d, int npeers, const void* bias,
                                       void* stream) {
-    // The epilogue writes D and every peer buffer with 16-byte stores (TMA for
-    // D, plain vector stores over NVLink for the peers): a misaligned peer
-    // address or row stride would fault on the GPU, so it is refused here,
-    // before anything is looked up or launched.
+    // The epilogue writes D and every peer buffer with TMA stores, whose tensor
+    // maps need 16-byte aligned rows: a misaligned peer address or row stride
+    // is refused here, before anything is looked up or launched.
     if (peer_d && npeers >= 1 && npeers <= 7) {
         bool aligned = ldd % 8 == 0 && (reinterpret_cast<uintptr_t>(D) & 15) == 0;
         for (int i = 0; i < npeers && aligned; ++i)

@@ -127,12 +127,10 @@ struct Params {
     int npeers;
 };
 
-// Output tensor maps of the peer buffers (column-parallel mode); all zero and
-// unused otherwise.  map: 32 x 32 boxes (the last tile's chunks); map64:
-// 16 x 64 boxes (every other tile's pieces).
+// Output tensor maps of the peer buffers (column-parallel mode; 16 x 64
+// boxes like the local one); all zero and unused otherwise.
 struct PeerMaps {
     CUtensorMap map[kMaxPeers];
-    CUtensorMap map64[kMaxPeers];
 };
 
 // Tile t -> (row tile, column tile) in groups of kTileGroupRows rows of A: the
@@ -278,32 +276,6 @@ __device__ __forceinline__ void convert_chunk(const Params& p, const uint32_t (&
     }
 }
 
-// Writes a converted chunk into the warp's 64B-swizzled staging buffer and
-// stores it with one TMA store (issued by a rotating lane), plus one TMA store
-// of the same staged chunk into each peer GPU's buffer (stores over NVLink; no
-// multicast, no load from another GPU).
-// `fresh`: the buffer has not been used since the operand ring went idle, so
-// no earlier store can still be reading it.
-__device__ __forceinline__ void store_staged_chunk(const Params& p, const CUtensorMap* tmap_d, const PeerMaps* pm,
-                                                   const uint32_t (&packed)[16], uint8_t* buf, int row0, int n,
-                                                   int lane, int chunk_iter, bool fresh = false) {
-    if (!fresh && lane == ((chunk_iter - 1) & 31)) ptx::bulk_wait_group_read<0>();
-    __syncwarp();
-    uint8_t* row = buf + 64 * lane;
-    const int sw = (lane >> 1) & 3;
-#pragma unroll
-    for (int u = 0; u < 4; ++u)
-        *reinterpret_cast<uint4*>(row + 16 * (u ^ sw)) =
-            make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
-    ptx::fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == (chunk_iter & 31)) {
-        ptx::tma_store_2d(tmap_d, buf, n, row0);
-        for (int d = 0; d < p.npeers; ++d) ptx::tma_store_2d(&pm->map[d], buf, n, row0);
-        ptx::bulk_commit_group();
-    }
-}
-
 // Stores a 16 x 64 piece of the output: rows [row0, row0 + 16) (held by lanes
 // 16 half .. 16 half + 15) of two adjacent converted 32-column chunks (lo:
 // columns [n, n + 32), hi: [n + 32, n + 64)).  The rows go into the warp's
@@ -311,10 +283,12 @@ __device__ __forceinline__ void store_staged_chunk(const Params& p, const CUtens
 // u ^ (r & 7): 8 consecutive rows on distinct banks), then one lane stores
 // the box locally and into every peer's buffer.  A piece has 128-byte rows:
 // SM-issued stores into another GPU's memory reach ~640 GB/s in each
-// direction at once with rows of 128 bytes or more, ~430 GB/s with the
-// 64-byte rows of a 32 x 32 chunk (measured on B200, two GPUs).  Same
-// rotating-lane protocol as store_staged_chunk.
-__device__ __forceinline__ void store_piece(const Params& p, const CUtensorMap* tmap_d64, const PeerMaps* pm,
+// direction at once with rows of 128 bytes or more, ~430 GB/s with 64-byte
+// rows (measured on B200, two GPUs).  One thread's TMA copies run one after
+// another (~0.4 us each), so piece i is stored by lane i % 32, and the lane
+// that stored the buffer's previous contents (piece i - 1) first waits until
+// that store has read it.
+__device__ __forceinline__ void store_piece(const Params& p, const CUtensorMap* tmap_d, const PeerMaps* pm,
                                             const uint32_t (&lo)[16], const uint32_t (&hi)[16], uint8_t* buf,
                                             int row0, int n, int half, int lane, int chunk_iter) {
     if (lane == ((chunk_iter - 1) & 31)) ptx::bulk_wait_group_read<0>();
@@ -333,8 +307,8 @@ __device__ __forceinline__ void store_piece(const Params& p, const CUtensorMap* 
     ptx::fence_proxy_async_smem();
     __syncwarp();
     if (lane == (chunk_iter & 31)) {
-        ptx::tma_store_2d(tmap_d64, buf, n, row0);
-        for (int d = 0; d < p.npeers; ++d) ptx::tma_store_2d(&pm->map64[d], buf, n, row0);
+        ptx::tma_store_2d(tmap_d, buf, n, row0);
+        for (int d = 0; d < p.npeers; ++d) ptx::tma_store_2d(&pm->map[d], buf, n, row0);
         ptx::bulk_commit_group();
     }
 }
@@ -655,8 +629,8 @@ struct PairCfg {
     // always brings the same bytes: those of both CTAs land on CTA 0's barrier.
     static constexpr uint32_t TX_BYTES = 2u * STAGE_BYTES;
     static constexpr int BAR_BYTES = 256;
-    // Epilogue staging: one 2 KB BF16 buffer (a 16 x 64 piece or a 32 x 32
-    // chunk) and the tile's BF16 bias per epilogue warp.
+    // Epilogue staging: one 2 KB BF16 buffer (a 16 x 64 piece) and the tile's
+    // BF16 bias per epilogue warp.
     static constexpr int EPI_BYTES = kPairEpiWarps * 2048;
     static constexpr int BIAS_BYTES = kPairEpiWarps * TW * 2;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + BIAS_BYTES + BAR_BYTES + 1024;
@@ -666,7 +640,7 @@ struct PairCfg {
     static constexpr uint32_t TMEM_SFB = TMEM_SFA + 4 * kKbPerStage;
     static_assert(B_SUB_BYTES % 1024 == 0 && B_SUB1_BYTES % 1024 == 0, "B stage must keep the 128B-swizzle alignment");
     static_assert(STAGE_BYTES % 1024 == 0, "epilogue buffers must stay 1024-byte aligned");
-    static_assert(STAGES * STAGE_BYTES >= 4 * (TW / 32) * 2048, "the idle ring stages every chunk of the last tile");
+    static_assert(STAGES * STAGE_BYTES >= 4 * (TW / 64) * 4096, "the idle ring stages all of the last tile");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
     static_assert(TMEM_SFA + SF_COLS <= kTmemCols, "TMEM budget exceeded");
 };
@@ -688,33 +662,58 @@ constexpr int kPairFirstProducer = 9;
 // Epilogue of a CTA pair's last tile by a team of warps per TMEM lane
 // quadrant q: the two epilogue warps q and q + 4 (members 0, 1) and the warps
 // whose roles have ended (8 and 12 on quadrant 0, 9, 10, 11 on quadrants 1-3).
-// Member ti of ts takes 32-column chunks c = ti, ti + ts, ...
-// The tile's BF16 bias was staged by epilogue warp q (chunk c at uint4
-// offset 4 c).  tq: TMEM address of the quadrant's accumulator; ring:
-// the operand ring, idle once the last tile's MMAs have completed, in which
-// chunk c of quadrant q is staged in a 2 KB slot of its own (q * CH + c), so no
-// chunk waits for an earlier TMA store to finish reading its buffer; m: this
-// lane's output row.
+// Member ti of ts takes the 64-column super-chunks s = ti, ti + ts, ...: it
+// converts both 32-column halves, stages the quadrant's 32 rows of the
+// super-chunk in a 4 KB slot of its own in the operand ring (idle once the
+// last tile's MMAs have completed; slot q * S + s, 128-byte swizzle), so no
+// store waits for an earlier one to finish reading, and stores them as two
+// 16 x 64 pieces (128-byte rows).  The tile's BF16 bias was staged by epilogue
+// warp q (chunk c at uint4 offset 4 c).  tq: TMEM address of the quadrant's
+// accumulator; m: this lane's output row.
 template <int TW>
 __device__ __forceinline__ void team_epilogue(const Params& p, const CUtensorMap* tmap_d, const PeerMaps* pm,
-                                              uint32_t tq,
-                                              const uint4* sBias, int q, int ti, int ts, uint8_t* ring,
+                                              uint32_t tq, const uint4* sBias, int q, int ti, int ts, uint8_t* ring,
                                               int& chunk_iter, int m, int n0, int lane) {
-    constexpr int CH = TW / 32;
+    constexpr int S = TW / 64;
+    const uint4* qbias = sBias + q * (TW / 8);
+    const int row0 = m - lane;  // the warp's first row
 #pragma unroll 1
-    for (int c = ti; c < CH; c += ts) {
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(tq + 32 * c, r);
+    for (int s = ti; s < S; s += ts) {
+        uint32_t ra[32], rb[32];
+        ptx::tmem_ld_32x32b_x32(tq + 64 * s, ra);
+        ptx::tmem_ld_32x32b_x32(tq + 64 * s + 32, rb);
         ptx::tmem_ld_wait();
-        if (n0 + 32 * c >= p.n_out) continue;
+        const int nc = n0 + 64 * s;
+        if (nc >= p.n_out) continue;
         if (p.tma_store) {
+            if (row0 >= p.m) continue;  // the warp's 32 rows start past D
+            uint8_t* slot = ring + (size_t)(q * S + s) * 4096;
+            // Row `lane` starts 128-byte aligned: unit u ^ (lane & 7) of it is at
+            // (row + 16 (lane & 7)) ^ 16 u.
+            const uint32_t a = ptx::smem_u32(slot) + 128u * lane + 16u * (lane & 7u);
             uint32_t pk[16];
-            convert_chunk(p, r, sBias + q * (TW / 8) + 4 * c, pk);
-            if (m - lane < p.m)  // the warp's 32 rows start inside D
-                store_staged_chunk(p, tmap_d, pm, pk, ring + (size_t)(q * CH + c) * 2048, m - lane, n0 + 32 * c,
-                                   lane, chunk_iter++, true);
+            convert_chunk(p, ra, qbias + 8 * s, pk);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) ptx::st_shared_v4(a ^ (16u * u), pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+            convert_chunk(p, rb, qbias + 8 * s + 4, pk);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                ptx::st_shared_v4(a ^ (16u * (u + 4)), pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+            ptx::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == (chunk_iter & 31)) {
+                ptx::tma_store_2d(tmap_d, slot, nc, row0);
+                for (int d = 0; d < p.npeers; ++d) ptx::tma_store_2d(&pm->map[d], slot, nc, row0);
+                if (row0 + 16 < p.m) {
+                    ptx::tma_store_2d(tmap_d, slot + 2048, nc, row0 + 16);
+                    for (int d = 0; d < p.npeers; ++d) ptx::tma_store_2d(&pm->map[d], slot + 2048, nc, row0 + 16);
+                }
+                ptx::bulk_commit_group();
+            }
+            ++chunk_iter;
         } else if (m < p.m) {
-            store_chunk(p, r, m, n0 + 32 * c);
+            store_chunk(p, ra, m, nc);
+            if (nc + 32 < p.n_out) store_chunk(p, rb, m, nc + 32);
         }
     }
 }
@@ -724,8 +723,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     nvf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_b1,
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-                          const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ CUtensorMap tmap_d64,
-                          const __grid_constant__ Params p, const __grid_constant__ PeerMaps pm) {
+                          const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ Params p,
+                          const __grid_constant__ PeerMaps pm) {
     using C = PairCfg<BN, STAGES, NSUB, BN1>;
     constexpr int TW = C::TW;
     constexpr int TILE_M = 2 * kBM;
@@ -773,10 +772,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         if (NSUB > 1) ptx::prefetch_tmap(&tmap_b1);
         ptx::prefetch_tmap(&tmap_sfa);
         ptx::prefetch_tmap(&tmap_sfb);
-        if (p.tma_store) {
-            ptx::prefetch_tmap(&tmap_d);
-            ptx::prefetch_tmap(&tmap_d64);
-        }
+        if (p.tma_store) ptx::prefetch_tmap(&tmap_d);
     }
     if (warp == kPairMmaWarp) {
         ptx::tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -1053,11 +1049,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     if (nc < p.n_out) {
                         if (!split) {
                             if (row0 < p.m)
-                                store_piece(p, &tmap_d64, &pm, pa, pb, epi, row0, nc, 0, lane, chunk_iter++);
+                                store_piece(p, &tmap_d, &pm, pa, pb, epi, row0, nc, 0, lane, chunk_iter++);
                             if (row0 + 16 < p.m)
-                                store_piece(p, &tmap_d64, &pm, pa, pb, epi, row0 + 16, nc, 1, lane, chunk_iter++);
+                                store_piece(p, &tmap_d, &pm, pa, pb, epi, row0 + 16, nc, 1, lane, chunk_iter++);
                         } else if (row0 + 16 * h < p.m) {
-                            store_piece(p, &tmap_d64, &pm, pa, pb, epi, row0 + 16 * h, nc, h, lane, chunk_iter++);
+                            store_piece(p, &tmap_d, &pm, pa, pb, epi, row0 + 16 * h, nc, h, lane, chunk_iter++);
                         }
                     }
                 } else {
@@ -1221,17 +1217,17 @@ bool make_scale_map(CUtensorMap* map, const void* base, long rows_pad, long k_pa
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// BF16 output D [m, n_out] with row stride ldd: 32 x 32 boxes with the 64-byte
-// swizzle, or (wide) 16-row x 64-column boxes with the 128-byte swizzle.
-bool make_output_map(CUtensorMap* map, void* base, long m, long n_out, long ldd, bool wide) {
+// BF16 output D [m, n_out] with row stride ldd: 16-row x 64-column boxes
+// (128-byte rows) with the 128-byte swizzle.
+bool make_output_map(CUtensorMap* map, void* base, long m, long n_out, long ldd) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)n_out, (cuuint64_t)m};
     const cuuint64_t strides[1] = {(cuuint64_t)(ldd * 2)};
-    const cuuint32_t box[2] = {wide ? 64u : 32u, wide ? 16u : 32u};
+    const cuuint32_t box[2] = {64, 16};
     const cuuint32_t estr[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               wide ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -1300,7 +1296,7 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const Q
     std::call_once(attr_once[dev & 63], [&] {
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     });
-    CUtensorMap ma, mb, mb1, msa, msb, md, md64;
+    CUtensorMap ma, mb, mb1, msa, msb, md;
     if (!make_operand_map(&ma, g.a_fp4, g.m_rows_pad, g.k_pad, kBM) ||
         !make_operand_map(&mb, g.b_fp4, g.n_rows_pad, g.k_pad, C::BH) ||
         !make_operand_map(&mb1, g.b_fp4, g.n_rows_pad, g.k_pad, C::BH1) ||
@@ -1310,20 +1306,15 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const Q
     Params p = make_params(g, C::TW, 2 * kBM);
     // D through TMA stores when C is not read and D's rows are 16-byte aligned.
     memset(&md, 0, sizeof(md));
-    memset(&md64, 0, sizeof(md64));
     const bool no_c = !g.c || g.beta == 0.0f;
     const bool d_ok = (reinterpret_cast<uintptr_t>(g.d) & 15) == 0 && g.ldd % 8 == 0;
-    if (no_c && d_ok && make_output_map(&md, g.d, g.m, g.n_out, g.ldd, false) &&
-        make_output_map(&md64, g.d, g.m, g.n_out, g.ldd, true))
-        p.tma_store = 1;
+    if (no_c && d_ok && make_output_map(&md, g.d, g.m, g.n_out, g.ldd)) p.tma_store = 1;
     PeerMaps pm;
     memset(&pm, 0, sizeof(pm));
     if (npeers > 0) {
         if (!p.tma_store || npeers > kMaxPeers) return cudaErrorNotSupported;
         for (int i = 0; i < npeers; ++i)
-            if (!make_output_map(&pm.map[i], peers[i], g.m, g.n_out, g.ldd, false) ||
-                !make_output_map(&pm.map64[i], peers[i], g.m, g.n_out, g.ldd, true))
-                return cudaErrorNotSupported;
+            if (!make_output_map(&pm.map[i], peers[i], g.m, g.n_out, g.ldd)) return cudaErrorNotSupported;
         p.npeers = npeers;
     }
     const int pairs = max_pairs(kernel, C::SMEM_BYTES, sms, kPairThreads);
@@ -1343,13 +1334,13 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const Q
         const cudaError_t e = quantize_units_launch(*qa, ready, ring, sms, stream);
         if (e != cudaSuccess) return e;
         const cudaError_t e2 = launch_dependent(kernel, dim3(grid), dim3(kPairThreads), C::SMEM_BYTES, stream, ma,
-                                                mb, mb1, msa, msb, md, md64, p, pm);
+                                                mb, mb1, msa, msb, md, p, pm);
         if (e2 != cudaSuccess)  // the quantizer ran alone: leave the counters zero for the next launch
             cudaMemsetAsync(ready, 0, (size_t)(p.ready_count + 1) * sizeof(uint32_t), stream);
         return e2;
     }
     return launch_dependent(kernel, dim3(grid), dim3(kPairThreads), C::SMEM_BYTES, stream, ma, mb, mb1, msa, msb, md,
-                            md64, p, pm);
+                            p, pm);
 }
 
 template <int BN, int STAGES, int CHUNKS>
