@@ -8,7 +8,11 @@
 // IPC), then waits until slot [peer_rank[i]] of this rank's own flag array has
 // reached `epoch`.  Launched on the stream right after the GEMM, so the GEMM's
 // stores precede the signal; the work after it on the stream sees every
-// peer's stores.  Epochs only grow (every rank counts its calls the same way),
+// peer's stores.  It is launched with programmatic stream serialization: the
+// block is placed while the GEMM still runs and waits (griddepcontrol.wait)
+// for the GEMM grid to complete, which saves a kernel launch gap per linear;
+// the kernel behind it may be placed early the same way and waits for this
+// one to complete.  Epochs only grow (every rank counts its calls the same way),
 // so a flag array is never reset.  The wait is bounded: after kPeerWaitNs
 // (10 s: the peers' hosts may run some seconds behind, e.g. while they build
 // their caches) it records kErrPeerBarrierTimeout in the device error word and
@@ -36,6 +40,8 @@ struct PeerFlags {
 
 __global__ void peer_barrier_kernel(const unsigned long long* my_flags, const __grid_constant__ PeerFlags pf,
                                     int npeers, int my_rank, unsigned long long epoch, int* err) {
+    ptx::grid_dependency_wait();  // the GEMM before this kernel has completed
+    ptx::launch_dependents();
     const int i = threadIdx.x;
     if (i >= npeers) return;
     // Everything this GPU wrote before (the GEMM's stores into the peers'
@@ -78,7 +84,16 @@ FP4B_EXPORT int fp4b_peer_barrier(const void* my_flags, void* const* peer_flags,
         pf.flags[i] = static_cast<unsigned long long*>(peer_flags[i]);
         pf.rank[i] = peer_ranks[i];
     }
-    peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const unsigned long long*>(my_flags), pf, npeers, my_rank, epoch, device_error_word());
-    return launch_status(cudaGetLastError(), "fp4b_peer_barrier launch");
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return launch_status(cudaLaunchKernelEx(&cfg, peer_barrier_kernel, static_cast<const unsigned long long*>(my_flags),
+                                            pf, npeers, my_rank, epoch, device_error_word()),
+                         "fp4b_peer_barrier launch");
 }
