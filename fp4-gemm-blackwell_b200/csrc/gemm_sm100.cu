@@ -128,7 +128,7 @@ struct Params {
 };
 
 // Output tensor maps of the peer buffers (column-parallel mode; 16 x 64
-// boxes like the local one); all zero and unused otherwise.
+// boxes like the local pieces); all zero and unused otherwise.
 struct PeerMaps {
     CUtensorMap map[kMaxPeers];
 };
@@ -276,13 +276,43 @@ __device__ __forceinline__ void convert_chunk(const Params& p, const uint32_t (&
     }
 }
 
+// Epilogue of one 32 x 32 chunk through shared memory (the single-GPU form):
+// thread t's converted row goes into the warp's 2 KB buffer in the TMA 64-byte
+// swizzle (16-byte unit u of row r at unit u ^ ((r >> 1) & 3), which keeps the
+// 16-byte shared stores of 8 consecutive rows on distinct banks), then one
+// lane stores the box [row0, row0 + 32) x [n, n + 32) with TMA; rows past M
+// and columns past N are clipped by the tensor map.  One thread's TMA copies
+// run one after another (~0.4 us each), so chunk i is stored by lane i % 32,
+// and the lane that stored the buffer's previous contents (chunk i - 1) first
+// waits until that store has read it.  `fresh`: the buffer has not been used
+// since the operand ring went idle, so no earlier store can still read it.
+__device__ __forceinline__ void store_staged_chunk(const CUtensorMap* tmap_d, const uint32_t (&packed)[16],
+                                                   uint8_t* buf, int row0, int n, int lane, int chunk_iter,
+                                                   bool fresh = false) {
+    if (!fresh && lane == ((chunk_iter - 1) & 31)) ptx::bulk_wait_group_read<0>();
+    __syncwarp();
+    uint8_t* row = buf + 64 * lane;
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(row + 16 * (u ^ sw)) =
+            make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == (chunk_iter & 31)) {
+        ptx::tma_store_2d(tmap_d, buf, n, row0);
+        ptx::bulk_commit_group();
+    }
+}
+
 // Stores a 16 x 64 piece of the output: rows [row0, row0 + 16) (held by lanes
 // 16 half .. 16 half + 15) of two adjacent converted 32-column chunks (lo:
 // columns [n, n + 32), hi: [n + 32, n + 64)).  The rows go into the warp's
 // 2 KB buffer in the TMA 128-byte swizzle (16-byte unit u of row r at unit
 // u ^ (r & 7): 8 consecutive rows on distinct banks), then one lane stores
-// the box locally and into every peer's buffer.  A piece has 128-byte rows:
-// SM-issued stores into another GPU's memory reach ~640 GB/s in each
+// the box locally and into every peer's buffer (the column-parallel form).  A
+// piece has 128-byte rows: SM-issued stores into another GPU's memory reach
+// ~640 GB/s in each
 // direction at once with rows of 128 bytes or more, ~430 GB/s with 64-byte
 // rows (measured on B200, two GPUs).  One thread's TMA copies run one after
 // another (~0.4 us each), so piece i is stored by lane i % 32, and the lane
@@ -629,8 +659,8 @@ struct PairCfg {
     // always brings the same bytes: those of both CTAs land on CTA 0's barrier.
     static constexpr uint32_t TX_BYTES = 2u * STAGE_BYTES;
     static constexpr int BAR_BYTES = 256;
-    // Epilogue staging: one 2 KB BF16 buffer (a 16 x 64 piece) and the tile's
-    // BF16 bias per epilogue warp.
+    // Epilogue staging: one 2 KB BF16 buffer (a 32 x 32 chunk or a 16 x 64
+    // piece) and room for the tile's BF16 bias per epilogue warp.
     static constexpr int EPI_BYTES = kPairEpiWarps * 2048;
     static constexpr int BIAS_BYTES = kPairEpiWarps * TW * 2;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + BIAS_BYTES + BAR_BYTES + 1024;
@@ -662,18 +692,46 @@ constexpr int kPairFirstProducer = 9;
 // Epilogue of a CTA pair's last tile by a team of warps per TMEM lane
 // quadrant q: the two epilogue warps q and q + 4 (members 0, 1) and the warps
 // whose roles have ended (8 and 12 on quadrant 0, 9, 10, 11 on quadrants 1-3).
-// Member ti of ts takes the 64-column super-chunks s = ti, ti + ts, ...: it
-// converts both 32-column halves, stages the quadrant's 32 rows of the
-// super-chunk in a 4 KB slot of its own in the operand ring (idle once the
-// last tile's MMAs have completed; slot q * S + s, 128-byte swizzle), so no
-// store waits for an earlier one to finish reading, and stores them as two
-// 16 x 64 pieces (128-byte rows).  The tile's BF16 bias was staged by epilogue
-// warp q (chunk c at uint4 offset 4 c).  tq: TMEM address of the quadrant's
-// accumulator; m: this lane's output row.
+// The operand ring is idle once the last tile's MMAs have completed: every
+// chunk gets a staging slot of its own there, so no store waits for an earlier
+// one to finish reading.  tq: TMEM address of the quadrant's accumulator; m:
+// this lane's output row.
+// Single-GPU form: member ti of ts takes the 32-column chunks c = ti, ti + ts,
+// ... (slot q * CH + c, 2 KB); chunk c's BF16 bias was staged by epilogue warp
+// q + 4 (c & 1) (uint4 offset 4 c).
 template <int TW>
-__device__ __forceinline__ void team_epilogue(const Params& p, const CUtensorMap* tmap_d, const PeerMaps* pm,
-                                              uint32_t tq, const uint4* sBias, int q, int ti, int ts, uint8_t* ring,
-                                              int& chunk_iter, int m, int n0, int lane) {
+__device__ __forceinline__ void team_epilogue_chunks(const Params& p, const CUtensorMap* tmap_d, uint32_t tq,
+                                                     const uint4* sBias, int q, int ti, int ts, uint8_t* ring,
+                                                     int& chunk_iter, int m, int n0, int lane) {
+    constexpr int CH = TW / 32;
+#pragma unroll 1
+    for (int c = ti; c < CH; c += ts) {
+        uint32_t r[32];
+        ptx::tmem_ld_32x32b_x32(tq + 32 * c, r);
+        ptx::tmem_ld_wait();
+        if (n0 + 32 * c >= p.n_out) continue;
+        if (p.tma_store) {
+            uint32_t pk[16];
+            convert_chunk(p, r, sBias + (q + 4 * (c & 1)) * (TW / 8) + 4 * c, pk);
+            if (m - lane < p.m)  // the warp's 32 rows start inside D
+                store_staged_chunk(tmap_d, pk, ring + (size_t)(q * CH + c) * 2048, m - lane, n0 + 32 * c, lane,
+                                   chunk_iter++, true);
+        } else if (m < p.m) {
+            store_chunk(p, r, m, n0 + 32 * c);
+        }
+    }
+}
+
+// Column-parallel form (TMA stores, peers): member ti of ts takes the
+// 64-column super-chunks s = ti, ti + ts, ...: it converts both 32-column
+// halves, stages the quadrant's 32 rows of the super-chunk in slot q * S + s
+// (4 KB, 128-byte swizzle) and stores them as two 16 x 64 pieces (128-byte
+// rows), locally and into every peer's buffer.  The tile's BF16 bias was
+// staged whole by epilogue warp q (chunk c at uint4 offset 4 c).
+template <int TW>
+__device__ __forceinline__ void team_epilogue_pieces(const Params& p, const CUtensorMap* tmap_d, const PeerMaps* pm,
+                                                     uint32_t tq, const uint4* sBias, int q, int ti, int ts,
+                                                     uint8_t* ring, int& chunk_iter, int m, int n0, int lane) {
     constexpr int S = TW / 64;
     const uint4* qbias = sBias + q * (TW / 8);
     const int row0 = m - lane;  // the warp's first row
@@ -718,13 +776,13 @@ __device__ __forceinline__ void team_epilogue(const Params& p, const CUtensorMap
     }
 }
 
-template <int BN, int STAGES, bool AWAIT, int NSUB, int BN1>
+template <int BN, int STAGES, bool AWAIT, int NSUB, int BN1, bool PIECES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     nvf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_b1,
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-                          const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ Params p,
-                          const __grid_constant__ PeerMaps pm) {
+                          const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ CUtensorMap tmap_d64,
+                          const __grid_constant__ Params p, const __grid_constant__ PeerMaps pm) {
     using C = PairCfg<BN, STAGES, NSUB, BN1>;
     constexpr int TW = C::TW;
     constexpr int TILE_M = 2 * kBM;
@@ -772,7 +830,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         if (NSUB > 1) ptx::prefetch_tmap(&tmap_b1);
         ptx::prefetch_tmap(&tmap_sfa);
         ptx::prefetch_tmap(&tmap_sfb);
-        if (p.tma_store) ptx::prefetch_tmap(&tmap_d);
+        if (p.tma_store) {
+            ptx::prefetch_tmap(&tmap_d);
+            if constexpr (PIECES) ptx::prefetch_tmap(&tmap_d64);
+        }
     }
     if (warp == kPairMmaWarp) {
         ptx::tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -966,8 +1027,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         }
     } else {
         // ------------------------------------------------------------ epilogue (both CTAs)
+        // Single-GPU form (!PIECES): warp w stores the 32-column chunks
+        // c = h, h + 2, ... as 32 x 32 boxes.  Column-parallel form: the 64-column
+        // super-chunks s = h, h + 2, ... as 16 x 64 pieces (128-byte rows for the
+        // stores over NVLink); with an odd count the last super-chunk is split by
+        // rows, warp w storing rows 16 h .. 16 h + 15 of it.  (Pieces cost the
+        // single-GPU GEMM 1-5 %: half the lanes stage each piece; and one kernel
+        // holding both forms spilled registers on the 384-wide tile.)
         const int q = warp & 3;   // TMEM lane quadrant
-        const int h = warp >> 2;  // super-chunks s = h, h + 2, ...
+        const int h = warp >> 2;
+        constexpr bool pieces = PIECES;
+        constexpr int kMyChunks = TW / 64;              // chunks per warp, single-GPU form
         constexpr int S = TW / 64;                      // 64-column super-chunks of a tile
         constexpr int kFull = S / 2;                    // whole super-chunks per warp
         constexpr bool kSplit = (S & 1) != 0;           // the last one is split by rows between the two warps
@@ -985,9 +1055,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             const int b = tile_iter % C::ACC_BUFS;
             const bool last_tile = t + npairs >= p.num_tiles;
             if (p.bias) {
+                // Chunk c's bias at wbias + 4 c: every chunk of the tile for the
+                // pieces, this warp's chunks for the single-GPU form.
                 __syncwarp();  // the previous tile's reads of wbias are done
+                if constexpr (pieces) {
 #pragma unroll
-                for (int c = 0; c < TW / 32; ++c) stage_bias(p, wbias + 4 * c, n0 + 32 * c, 32, lane);
+                    for (int c = 0; c < TW / 32; ++c) stage_bias(p, wbias + 4 * c, n0 + 32 * c, 32, lane);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < kMyChunks; ++j)
+                        stage_bias(p, wbias + 4 * (h + 2 * j), n0 + 32 * (h + 2 * j), 32, lane);
+                }
                 __syncwarp();
             }
             if (last_tile && lane == 0) ptx::mbar_arrive(bias_ready);
@@ -1009,13 +1087,67 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     }
                     break;
                 }
-                team_epilogue<TW>(p, &tmap_d, &pm, tmem + ((uint32_t)(q * 32) << 16) + b * TW, sBias, q, h,
-                                  q == 0 ? 4 : 3, smem, chunk_iter, m, n0, lane);
+                const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + b * TW;
+                if constexpr (pieces)
+                    team_epilogue_pieces<TW>(p, &tmap_d64, &pm, tq, sBias, q, h, q == 0 ? 4 : 3, smem, chunk_iter, m,
+                                             n0, lane);
+                else
+                    team_epilogue_chunks<TW>(p, &tmap_d, tq, sBias, q, h, q == 0 ? 4 : 3, smem, chunk_iter, m, n0,
+                                             lane);
                 continue;
             }
             // Only a later tile of this pair that reuses accumulator b waits for it.
             const bool release = t + C::ACC_BUFS * npairs < p.num_tiles;
-            // One super-chunk (two 32-column TMEM loads) per iteration: both halves
+            if constexpr (!pieces) {
+                // Chunks go two at a time: both are converted together (independent
+                // work for the warp's latency), then the next two TMEM loads are issued
+                // into the freed registers while the converted pair is stored.
+                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + b * TW + 32 * h;
+                uint32_t ra[32], rb[32];
+                ptx::tmem_ld_32x32b_x32(tbase, ra);
+                if (kMyChunks > 1) ptx::tmem_ld_32x32b_x32(tbase + 64, rb);
+#pragma unroll
+                for (int j = 0; j < kMyChunks; j += 2) {
+                    const bool two = j + 1 < kMyChunks;
+                    const int c0 = h + 2 * j, c1 = c0 + 2;
+                    const bool in0 = n0 + 32 * c0 < p.n_out, in1 = two && n0 + 32 * c1 < p.n_out;
+                    ptx::tmem_ld_wait();
+                    if (p.tma_store) {
+                        uint32_t pa[16], pb[16];
+                        convert_chunk(p, ra, wbias + 4 * c0, pa);
+                        if (two) convert_chunk(p, rb, wbias + 4 * c1, pb);
+                        if (j + 2 < kMyChunks) {
+                            ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 2), ra);
+                            if (j + 3 < kMyChunks) ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 3), rb);
+                        } else if (release) {
+                            // Every TMEM read of this accumulator is done: hand it back to the MMA issuer.
+                            ptx::tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) ptx::mbar_arrive_cluster(acc_empty0 + (uint32_t)b * 8u);
+                        }
+                        if (m - lane < p.m) {  // the warp's 32 rows start inside D
+                            if (in0) store_staged_chunk(&tmap_d, pa, epi, m - lane, n0 + 32 * c0, lane, chunk_iter++);
+                            if (in1) store_staged_chunk(&tmap_d, pb, epi, m - lane, n0 + 32 * c1, lane, chunk_iter++);
+                        }
+                    } else {
+                        if (m < p.m) {
+                            if (in0) store_chunk(p, ra, m, n0 + 32 * c0);
+                            if (in1) store_chunk(p, rb, m, n0 + 32 * c1);
+                        }
+                        if (j + 2 < kMyChunks) {
+                            ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 2), ra);
+                            if (j + 3 < kMyChunks) ptx::tmem_ld_32x32b_x32(tbase + 64 * (j + 3), rb);
+                        } else if (release) {
+                            ptx::tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) ptx::mbar_arrive_cluster(acc_empty0 + (uint32_t)b * 8u);
+                        }
+                    }
+                }
+                continue;
+            }
+            // Column-parallel form (TMA stores; launch_pair refuses peers without
+            // them).  One super-chunk (two 32-column TMEM loads) per iteration: both halves
             // are converted together (independent work for the warp's latency), then
             // the next super-chunk's loads are issued into the freed registers while
             // the converted one is stored.
@@ -1032,48 +1164,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 const int nsc = (j + 1 == kFull && kSplit) ? S - 1 : h + 2 * (j + 1);  // next iteration's
                 const int nc = n0 + 64 * sc;
                 ptx::tmem_ld_wait();
-                if (p.tma_store) {
-                    uint32_t pa[16], pb[16];
-                    const uint4* bsc = (kSplit && split) ? wbias + 8 * (S - 1) : wbh + 16 * j;  // chunks 2 sc, 2 sc + 1
-                    convert_chunk(p, ra, bsc, pa);
-                    convert_chunk(p, rb, bsc + 4, pb);
-                    if (j + 1 < kIters) {
-                        ptx::tmem_ld_32x32b_x32(tacc + 64 * nsc, ra);
-                        ptx::tmem_ld_32x32b_x32(tacc + 64 * nsc + 32, rb);
-                    } else if (release) {
-                        // Every TMEM read of this accumulator is done: hand it back to the MMA issuer.
-                        ptx::tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) ptx::mbar_arrive_cluster(acc_empty0 + (uint32_t)b * 8u);
-                    }
-                    if (nc < p.n_out) {
-                        if (!split) {
-                            if (row0 < p.m)
-                                store_piece(p, &tmap_d, &pm, pa, pb, epi, row0, nc, 0, lane, chunk_iter++);
-                            if (row0 + 16 < p.m)
-                                store_piece(p, &tmap_d, &pm, pa, pb, epi, row0 + 16, nc, 1, lane, chunk_iter++);
-                        } else if (row0 + 16 * h < p.m) {
-                            store_piece(p, &tmap_d, &pm, pa, pb, epi, row0 + 16 * h, nc, h, lane, chunk_iter++);
-                        }
-                    }
-                } else {
-                    if (m < p.m) {
-                        if (!split) {
-                            if (nc < p.n_out) store_chunk(p, ra, m, nc);
-                            if (nc + 32 < p.n_out) store_chunk(p, rb, m, nc + 32);
-                        } else if (h == 0) {
-                            if (nc < p.n_out) store_chunk(p, ra, m, nc);
-                        } else if (nc + 32 < p.n_out) {
-                            store_chunk(p, rb, m, nc + 32);
-                        }
-                    }
-                    if (j + 1 < kIters) {
-                        ptx::tmem_ld_32x32b_x32(tacc + 64 * nsc, ra);
-                        ptx::tmem_ld_32x32b_x32(tacc + 64 * nsc + 32, rb);
-                    } else if (release) {
-                        ptx::tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) ptx::mbar_arrive_cluster(acc_empty0 + (uint32_t)b * 8u);
+                uint32_t pa[16], pb[16];
+                const uint4* bsc = (kSplit && split) ? wbias + 8 * (S - 1) : wbh + 16 * j;  // chunks 2 sc, 2 sc + 1
+                convert_chunk(p, ra, bsc, pa);
+                convert_chunk(p, rb, bsc + 4, pb);
+                if (j + 1 < kIters) {
+                    ptx::tmem_ld_32x32b_x32(tacc + 64 * nsc, ra);
+                    ptx::tmem_ld_32x32b_x32(tacc + 64 * nsc + 32, rb);
+                } else if (release) {
+                    // Every TMEM read of this accumulator is done: hand it back to the MMA issuer.
+                    ptx::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive_cluster(acc_empty0 + (uint32_t)b * 8u);
+                }
+                if (nc < p.n_out) {
+                    if (!split) {
+                        if (row0 < p.m) store_piece(p, &tmap_d64, &pm, pa, pb, epi, row0, nc, 0, lane, chunk_iter++);
+                        if (row0 + 16 < p.m)
+                            store_piece(p, &tmap_d64, &pm, pa, pb, epi, row0 + 16, nc, 1, lane, chunk_iter++);
+                    } else if (row0 + 16 * h < p.m) {
+                        store_piece(p, &tmap_d64, &pm, pa, pb, epi, row0 + 16 * h, nc, h, lane, chunk_iter++);
                     }
                 }
             }
@@ -1110,8 +1220,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             ptx::tc_fence_after();
             // Every MMA has completed and no load is left: the operand ring is idle.
             int chunk_iter = 0;
-            team_epilogue<TW>(p, &tmap_d, &pm, tmem + ((uint32_t)(q * 32) << 16) + b * TW, sBias, q, ti,
-                              q == 0 ? 4 : 3, smem, chunk_iter, m, n0, lane);
+            const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + b * TW;
+            if constexpr (PIECES)
+                team_epilogue_pieces<TW>(p, &tmap_d64, &pm, tq, sBias, q, ti, q == 0 ? 4 : 3, smem, chunk_iter, m,
+                                         n0, lane);
+            else
+                team_epilogue_chunks<TW>(p, &tmap_d, tq, sBias, q, ti, q == 0 ? 4 : 3, smem, chunk_iter, m, n0,
+                                         lane);
             ptx::bulk_wait_group_all();
             if (p.npeers > 0) {
                 ptx::fence_proxy_async_global();
@@ -1217,17 +1332,18 @@ bool make_scale_map(CUtensorMap* map, const void* base, long rows_pad, long k_pa
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// BF16 output D [m, n_out] with row stride ldd: 16-row x 64-column boxes
-// (128-byte rows) with the 128-byte swizzle.
-bool make_output_map(CUtensorMap* map, void* base, long m, long n_out, long ldd) {
+// BF16 output D [m, n_out] with row stride ldd: 32 x 32 boxes with the 64-byte
+// swizzle (single-GPU chunks), or (wide) 16-row x 64-column boxes (128-byte
+// rows) with the 128-byte swizzle (column-parallel pieces).
+bool make_output_map(CUtensorMap* map, void* base, long m, long n_out, long ldd, bool wide) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)n_out, (cuuint64_t)m};
     const cuuint64_t strides[1] = {(cuuint64_t)(ldd * 2)};
-    const cuuint32_t box[2] = {64, 16};
+    const cuuint32_t box[2] = {wide ? 64u : 32u, wide ? 16u : 32u};
     const cuuint32_t estr[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               wide ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -1285,18 +1401,18 @@ int max_pairs(K kernel, int smem, int sms, int threads) {
 // Shared memory of one SM (233472 bytes on B200) minus a CTA's reserved 1 KB.
 constexpr int kSmemPerSm = 233472;
 
-template <int BN, int STAGES, bool AWAIT = false, int NSUB = 1, int BN1 = BN>
+template <int BN, int STAGES, bool AWAIT = false, int NSUB = 1, int BN1 = BN, bool PIECES = false>
 cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const QuantizeArgs* qa = nullptr,
                         uint32_t* ready = nullptr, void* const* peers = nullptr, int npeers = 0) {
     using C = PairCfg<BN, STAGES, NSUB, BN1>;
-    auto kernel = nvf4_gemm_pair_kernel<BN, STAGES, AWAIT, NSUB, BN1>;
+    auto kernel = nvf4_gemm_pair_kernel<BN, STAGES, AWAIT, NSUB, BN1, PIECES>;
     static std::once_flag attr_once[64];
     int dev = 0;
     cudaGetDevice(&dev);
     std::call_once(attr_once[dev & 63], [&] {
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     });
-    CUtensorMap ma, mb, mb1, msa, msb, md;
+    CUtensorMap ma, mb, mb1, msa, msb, md, md64;
     if (!make_operand_map(&ma, g.a_fp4, g.m_rows_pad, g.k_pad, kBM) ||
         !make_operand_map(&mb, g.b_fp4, g.n_rows_pad, g.k_pad, C::BH) ||
         !make_operand_map(&mb1, g.b_fp4, g.n_rows_pad, g.k_pad, C::BH1) ||
@@ -1306,16 +1422,23 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const Q
     Params p = make_params(g, C::TW, 2 * kBM);
     // D through TMA stores when C is not read and D's rows are 16-byte aligned.
     memset(&md, 0, sizeof(md));
+    memset(&md64, 0, sizeof(md64));
     const bool no_c = !g.c || g.beta == 0.0f;
     const bool d_ok = (reinterpret_cast<uintptr_t>(g.d) & 15) == 0 && g.ldd % 8 == 0;
-    if (no_c && d_ok && make_output_map(&md, g.d, g.m, g.n_out, g.ldd)) p.tma_store = 1;
+    if (no_c && d_ok && make_output_map(&md, g.d, g.m, g.n_out, g.ldd, false) &&
+        make_output_map(&md64, g.d, g.m, g.n_out, g.ldd, true))
+        p.tma_store = 1;
     PeerMaps pm;
     memset(&pm, 0, sizeof(pm));
-    if (npeers > 0) {
-        if (!p.tma_store || npeers > kMaxPeers) return cudaErrorNotSupported;
-        for (int i = 0; i < npeers; ++i)
-            if (!make_output_map(&pm.map[i], peers[i], g.m, g.n_out, g.ldd)) return cudaErrorNotSupported;
-        p.npeers = npeers;
+    if constexpr (PIECES) {
+        if (npeers > 0) {
+            if (!p.tma_store || npeers > kMaxPeers) return cudaErrorNotSupported;
+            for (int i = 0; i < npeers; ++i)
+                if (!make_output_map(&pm.map[i], peers[i], g.m, g.n_out, g.ldd, true)) return cudaErrorNotSupported;
+            p.npeers = npeers;
+        }
+    } else if (npeers > 0) {
+        return cudaErrorNotSupported;  // peer stores need the column-parallel epilogue form
     }
     const int pairs = max_pairs(kernel, C::SMEM_BYTES, sms, kPairThreads);
     const int grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);
@@ -1334,13 +1457,13 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const Q
         const cudaError_t e = quantize_units_launch(*qa, ready, ring, sms, stream);
         if (e != cudaSuccess) return e;
         const cudaError_t e2 = launch_dependent(kernel, dim3(grid), dim3(kPairThreads), C::SMEM_BYTES, stream, ma,
-                                                mb, mb1, msa, msb, md, p, pm);
+                                                mb, mb1, msa, msb, md, md64, p, pm);
         if (e2 != cudaSuccess)  // the quantizer ran alone: leave the counters zero for the next launch
             cudaMemsetAsync(ready, 0, (size_t)(p.ready_count + 1) * sizeof(uint32_t), stream);
         return e2;
     }
     return launch_dependent(kernel, dim3(grid), dim3(kPairThreads), C::SMEM_BYTES, stream, ma, mb, mb1, msa, msb, md,
-                            p, pm);
+                            md64, p, pm);
 }
 
 template <int BN, int STAGES, int CHUNKS>
@@ -1457,11 +1580,11 @@ cudaError_t gemm_launch_peers(const GemmArgs& g, void* const* peers, int npeers,
     const char* force = getenv("FP4B_FORCE_BN");
     const int bn = force ? atoi(force) : choose_bn_pair(g.m, g.n_out, g.k_pad, sms);
     switch (bn) {
-        case 256: return launch_pair<256, 5, false>(g, stream, sms, nullptr, nullptr, peers, npeers);
-        case 192: return launch_pair<192, 6, false>(g, stream, sms, nullptr, nullptr, peers, npeers);
-        case 128: return launch_pair<128, 7, false>(g, stream, sms, nullptr, nullptr, peers, npeers);
-        case 384: return launch_pair<192, 4, false, 2>(g, stream, sms, nullptr, nullptr, peers, npeers);
-        case 320: return launch_pair<128, 4, false, 2, 192>(g, stream, sms, nullptr, nullptr, peers, npeers);
+        case 256: return launch_pair<256, 5, false, 1, 256, true>(g, stream, sms, nullptr, nullptr, peers, npeers);
+        case 192: return launch_pair<192, 6, false, 1, 192, true>(g, stream, sms, nullptr, nullptr, peers, npeers);
+        case 128: return launch_pair<128, 7, false, 1, 128, true>(g, stream, sms, nullptr, nullptr, peers, npeers);
+        case 384: return launch_pair<192, 4, false, 2, 192, true>(g, stream, sms, nullptr, nullptr, peers, npeers);
+        case 320: return launch_pair<128, 4, false, 2, 192, true>(g, stream, sms, nullptr, nullptr, peers, npeers);
         default: return cudaErrorInvalidValue;
     }
 }
