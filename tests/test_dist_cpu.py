@@ -138,3 +138,33 @@ def test_row_chunks_partition_rows():
         assert ch[0][0] == 0 and ch[-1][1] == m and len(ch) <= 4
         for (a0, a1), (b0, b1) in zip(ch, ch[1:]):
             assert a1 == b0 and (a1 - a0) % D.TILE == 0 and a1 - a0 >= 1024
+
+
+def _layer_stub(mode, n, world=2, bias_ok=True):
+    # The mode decisions of ColumnParallelFP4Linear are host logic; a stub
+    # with just the fields they read stands in for a layer (which needs GPUs).
+    lin = object.__new__(D.ColumnParallelFP4Linear)
+    lin.mode, lin.n, lin.world, lin._bias_ok = mode, n, world, bias_ok
+    lin.device = torch.device("cuda", 0)
+    return lin
+
+
+def test_column_parallel_mode_choice():
+    auto = _layer_stub("auto", 2880)
+    # auto: the GEMM epilogue stores to the peers where the CTA-pair kernel runs
+    # (M > 128) and rows are 16-byte aligned; else copy-engine pushes.
+    assert auto.uses_p2p(129) and auto._epilogue(129)
+    assert auto.uses_p2p(128) and not auto._epilogue(128)
+    assert auto.uses_p2p(1) and not auto._epilogue(1)
+    odd = _layer_stub("auto", 2884 + 1)
+    assert odd.uses_p2p(4096) and not odd._epilogue(4096)
+    ce = _layer_stub("p2p", 2880)
+    assert ce.uses_p2p(4096) and not ce._epilogue(4096)
+    ep = _layer_stub("epilogue", 2880)
+    assert ep.uses_p2p(4096) and ep._epilogue(4096)
+    assert not ep.uses_p2p(128)  # falls back to the all-gather
+    assert not _layer_stub("nccl", 2880).uses_p2p(4096)
+    assert not _layer_stub("auto", 2880, world=1).uses_p2p(4096)
+    assert not _layer_stub("auto", 2880, bias_ok=False).uses_p2p(4096)  # an fp32 bias is added after a gather
+    with pytest.raises(ValueError):
+        D.ColumnParallelFP4Linear(torch.zeros(128, 128), mode="ring")
