@@ -704,20 +704,24 @@ __device__ __forceinline__ void team_epilogue_chunks(const Params& p, const CUte
                                                      const uint4* sBias, int q, int ti, int ts, uint8_t* ring,
                                                      int& chunk_iter, int m, int n0, int lane) {
     constexpr int CH = TW / 32;
+    // The next chunk's TMEM load is issued once this one is converted, so its
+    // latency overlaps the staging and the store.
+    uint32_t r[32];
+    if (ti < CH) ptx::tmem_ld_32x32b_x32(tq + 32 * ti, r);
 #pragma unroll 1
     for (int c = ti; c < CH; c += ts) {
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(tq + 32 * c, r);
         ptx::tmem_ld_wait();
-        if (n0 + 32 * c >= p.n_out) continue;
+        const bool live = n0 + 32 * c < p.n_out;
         if (p.tma_store) {
             uint32_t pk[16];
             convert_chunk(p, r, sBias + (q + 4 * (c & 1)) * (TW / 8) + 4 * c, pk);
-            if (m - lane < p.m)  // the warp's 32 rows start inside D
+            if (c + ts < CH) ptx::tmem_ld_32x32b_x32(tq + 32 * (c + ts), r);
+            if (live && m - lane < p.m)  // the warp's 32 rows start inside D
                 store_staged_chunk(tmap_d, pk, ring + (size_t)(q * CH + c) * 2048, m - lane, n0 + 32 * c, lane,
                                    chunk_iter++, true);
-        } else if (m < p.m) {
-            store_chunk(p, r, m, n0 + 32 * c);
+        } else {
+            if (live && m < p.m) store_chunk(p, r, m, n0 + 32 * c);
+            if (c + ts < CH) ptx::tmem_ld_32x32b_x32(tq + 32 * (c + ts), r);
         }
     }
 }
@@ -735,25 +739,36 @@ __device__ __forceinline__ void team_epilogue_pieces(const Params& p, const CUte
     constexpr int S = TW / 64;
     const uint4* qbias = sBias + q * (TW / 8);
     const int row0 = m - lane;  // the warp's first row
+    // The next super-chunk's TMEM loads are issued once this one is converted,
+    // so their latency overlaps the staging and the stores.  (Column-parallel
+    // launches always have TMA stores.)
+    uint32_t ra[32], rb[32];
+    if (ti < S) {
+        ptx::tmem_ld_32x32b_x32(tq + 64 * ti, ra);
+        ptx::tmem_ld_32x32b_x32(tq + 64 * ti + 32, rb);
+    }
 #pragma unroll 1
     for (int s = ti; s < S; s += ts) {
-        uint32_t ra[32], rb[32];
-        ptx::tmem_ld_32x32b_x32(tq + 64 * s, ra);
-        ptx::tmem_ld_32x32b_x32(tq + 64 * s + 32, rb);
         ptx::tmem_ld_wait();
         const int nc = n0 + 64 * s;
-        if (nc >= p.n_out) continue;
-        if (p.tma_store) {
-            if (row0 >= p.m) continue;  // the warp's 32 rows start past D
-            uint8_t* slot = ring + (size_t)(q * S + s) * 4096;
-            // Row `lane` starts 128-byte aligned: unit u ^ (lane & 7) of it is at
-            // (row + 16 (lane & 7)) ^ 16 u.
-            const uint32_t a = ptx::smem_u32(slot) + 128u * lane + 16u * (lane & 7u);
-            uint32_t pk[16];
+        const bool live = nc < p.n_out && row0 < p.m;  // columns and the warp's first row inside D
+        uint8_t* slot = ring + (size_t)(q * S + s) * 4096;
+        // Row `lane` starts 128-byte aligned: unit u ^ (lane & 7) of it is at
+        // (row + 16 (lane & 7)) ^ 16 u.
+        const uint32_t a = ptx::smem_u32(slot) + 128u * lane + 16u * (lane & 7u);
+        uint32_t pk[16];
+        if (live) {
             convert_chunk(p, ra, qbias + 8 * s, pk);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) ptx::st_shared_v4(a ^ (16u * u), pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+            for (int u = 0; u < 4; ++u)
+                ptx::st_shared_v4(a ^ (16u * u), pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
             convert_chunk(p, rb, qbias + 8 * s + 4, pk);
+        }
+        if (s + ts < S) {
+            ptx::tmem_ld_32x32b_x32(tq + 64 * (s + ts), ra);
+            ptx::tmem_ld_32x32b_x32(tq + 64 * (s + ts) + 32, rb);
+        }
+        if (live) {
 #pragma unroll
             for (int u = 0; u < 4; ++u)
                 ptx::st_shared_v4(a ^ (16u * (u + 4)), pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
@@ -769,9 +784,6 @@ __device__ __forceinline__ void team_epilogue_pieces(const Params& p, const CUte
                 ptx::bulk_commit_group();
             }
             ++chunk_iter;
-        } else if (m < p.m) {
-            store_chunk(p, ra, m, nc);
-            if (nc + 32 < p.n_out) store_chunk(p, rb, m, nc + 32);
         }
     }
 }
