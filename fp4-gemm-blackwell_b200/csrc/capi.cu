@@ -394,9 +394,9 @@ FP4B_EXPORT int fp4b_run_cached_peers(const void* A, int m, int k_in, int lda, c
         set_last_error("null or invalid cache handle");
         return -1;
     }
-    if (!A || !D || m <= 128 || k_in <= 0 || k_in > c->K || lda < k_in || n_out <= 0 || n_out > c->N ||
+    if (!A || !D || m <= 0 || k_in <= 0 || k_in > c->K || lda < k_in || n_out <= 0 || n_out > c->N ||
         !peer_d || npeers < 1 || npeers > 7) {
-        set_last_error("fp4b_run_cached_peers: bad arguments (m=%d must exceed 128, 1..7 peers)", m);
+        set_last_error("fp4b_run_cached_peers: bad arguments (m=%d, 1..7 peers)", m);
         return -1;
     }
     const long m_pad = round_up(m, 128);

@@ -19,12 +19,13 @@ single-GPU kernels of ``fp4_gemm``:
       the GEMM tile by tile; a flag barrier on the GPU (``PeerFlagBarrier``:
       one warp signals every peer and waits for every peer's signal) then
       orders the ranks.  No gather buffer, no re-layout, no collective.
-      Needs M > 128 (the CTA-pair kernel) and N a multiple of 8.
+      Needs N a multiple of 8.
     - "p2p": the same mapped buffers, but the GEMM writes only this rank's
       buffer, in row chunks, and a side stream pushes each finished chunk to
       every peer with a strided copy-engine copy while the next chunk is
       computed; then the flag barrier.  Any M.
-    - "auto" (the default): "epilogue" where it applies, else "p2p".
+    - "auto" (the default): "epilogue" where it applies (N a multiple of 8),
+      else "p2p".
     - "nccl": one NCCL all-gather of equal-size, zero-padded slices and a
       re-layout.
 
@@ -235,14 +236,14 @@ class ColumnParallelFP4Linear:
         if self.mode == "nccl" or self.world == 1 or self.device.type != "cuda" or not self._bias_ok or m <= 0:
             return False
         if self.mode == "epilogue":
-            return m > 128 and self.n % 8 == 0
+            return self.n % 8 == 0
         return True
 
     def _epilogue(self, m: int) -> bool:
         """Whether a mapped-buffer forward of M rows has the GEMM epilogue store the
-        peers' copies ("epilogue", and "auto" where the CTA-pair kernel runs)
+        peers' copies ("epilogue", and "auto" where the rows are 16-byte aligned)
         rather than the copy engine ("p2p")."""
-        return self.mode == "epilogue" or (self.mode == "auto" and m > 128 and self.n % 8 == 0)
+        return self.mode == "epilogue" or (self.mode == "auto" and self.n % 8 == 0)
 
     def _ensure_buffers(self, m: int):
         import fp4_gemm

@@ -97,9 +97,8 @@ int fp4b_version(void);
 /* Output columns per tile the GEMM picks for an M x N x K problem (K padded to
  * 128) on a device with `sms` SMs, from its time model and without the
  * FP4B_PAIR / FP4B_FORCE_BN overrides: 128 / 192 / 256 (one MMA per k-block),
- * 320 (128 + 192) or 384 (192 + 192) on CTA pairs when M > 128, else the
- * one-CTA kernel's 128 / 192 / 256.  -1 on bad arguments.  Host only: no
- * device work, no GPU needed. */
+ * 320 (128 + 192) or 384 (192 + 192), on CTA pairs at every M.  -1 on bad
+ * arguments.  Host only: no device work, no GPU needed. */
 int fp4b_gemm_tile_width(int m, int n, int k, int sms);
 
 /* Message of the last failed call on this host thread ("" if none). */
@@ -221,7 +220,7 @@ int fp4b_run_cached_noalloc(const void* A_bf16, int m, int k_in, int lda, const 
  * GPUs' [.., ldd] BF16 outputs mapped with fp4b_ipc_open_handle, each already
  * offset to this rank's first column) with NVLink stores.  The caller orders
  * the ranks after the call (fp4b_peer_barrier on the same stream, or a
- * collective).  m > 128, no C.  D and every peer_d[i] must be 16-byte aligned
+ * collective).  No C.  D and every peer_d[i] must be 16-byte aligned
  * and ldd a multiple of 8 elements (the epilogue stores 16 bytes at a time);
  * otherwise -2 before any device work.  Asynchronous on `stream`; other return
  * codes as fp4b_run_cached_ex. */

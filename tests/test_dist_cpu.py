@@ -151,18 +151,17 @@ def _layer_stub(mode, n, world=2, bias_ok=True):
 
 def test_column_parallel_mode_choice():
     auto = _layer_stub("auto", 2880)
-    # auto: the GEMM epilogue stores to the peers where the CTA-pair kernel runs
-    # (M > 128) and rows are 16-byte aligned; else copy-engine pushes.
-    assert auto.uses_p2p(129) and auto._epilogue(129)
-    assert auto.uses_p2p(128) and not auto._epilogue(128)
-    assert auto.uses_p2p(1) and not auto._epilogue(1)
+    # auto: the GEMM epilogue stores to the peers where the output rows are
+    # 16-byte aligned (N a multiple of 8), at any M; else copy-engine pushes.
+    for m in (1, 128, 129, 8192):
+        assert auto.uses_p2p(m) and auto._epilogue(m)
     odd = _layer_stub("auto", 2884 + 1)
     assert odd.uses_p2p(4096) and not odd._epilogue(4096)
     ce = _layer_stub("p2p", 2880)
     assert ce.uses_p2p(4096) and not ce._epilogue(4096)
     ep = _layer_stub("epilogue", 2880)
-    assert ep.uses_p2p(4096) and ep._epilogue(4096)
-    assert not ep.uses_p2p(128)  # falls back to the all-gather
+    assert ep.uses_p2p(4096) and ep._epilogue(4096) and ep.uses_p2p(1)
+    assert not _layer_stub("epilogue", 2885).uses_p2p(4096)  # unaligned rows: the all-gather
     assert not _layer_stub("nccl", 2880).uses_p2p(4096)
     assert not _layer_stub("auto", 2880, world=1).uses_p2p(4096)
     assert not _layer_stub("auto", 2880, bias_ok=False).uses_p2p(4096)  # an fp32 bias is added after a gather

@@ -56,7 +56,7 @@ def _worker(rank, world, port, q):
         assert ep.uses_p2p(m)
         assert torch.equal(ep.forward(xd[:256]), single.forward(xd[:256]))
         assert torch.equal(ep.forward(xd), ref)
-        assert torch.equal(ep.forward(xd[:100]), single.forward(xd[:100]))  # M <= 128: all-gather
+        assert torch.equal(ep.forward(xd[:100]), single.forward(xd[:100]))  # M <= 128: a pair's second CTA is padding
         ep.free()
         ce = D.ColumnParallelFP4Linear(wd, bd, mode="p2p")  # copy-engine pushes
         assert ce.uses_p2p(m) and not ce._epilogue(m)
@@ -65,9 +65,10 @@ def _worker(rank, world, port, q):
         want_big = single.forward(big)
         assert torch.equal(ce.forward(big), want_big)
         assert torch.equal(tp.forward(big), want_big)  # auto: epilogue stores, several tiles per CTA pair
-        small = tp.forward(xd[:100])  # auto at M <= 128: copy-engine pushes
-        assert not tp._epilogue(100)
+        small = tp.forward(xd[:100])  # auto at M <= 128: the epilogue stores too
+        assert tp._epilogue(100)
         assert torch.equal(small, single.forward(xd[:100]))
+        assert torch.equal(ce.forward(xd[:100]), small)  # copy-engine pushes of a single row chunk
         ce.free()
         nc.free()
         r0, r1 = D.row_range(m, world, rank)

@@ -23,6 +23,8 @@ GUARD = 4096
 @pytest.mark.parametrize("pair,bn,m,n", [(0, 128, 100, 1000), (0, 256, 128, 1000), (1, 192, 300, 1000),
                                          (1, 256, 300, 1000), (1, 320, 300, 1000), (1, 384, 300, 1000),
                                          (1, 128, 4096, 1000), (1, 384, 8192, 1000),
+                                         # CTA pairs at M <= 128 (the default): the second CTA's rows are padding
+                                         (1, 128, 100, 1000), (1, 320, 1, 1000), (1, 192, 128, 1000),
                                          # more column tiles than CTA pairs: the ragged last row tile is
                                          # stored by the per-tile epilogue too, not only the last-tile team
                                          (1, 128, 300, 10000), (1, 192, 300, 14500), (1, 320, 300, 24000)])

@@ -51,7 +51,7 @@ def test_gemm_tile_width_model_decisions():
     # shapes it was fitted on, with B200's 148 SMs: the 320-wide two-MMA tile
     # for the headline (72 tiles on 74 CTA pairs), the 384-wide one for
     # short-K many-round shapes (config-5 gate_up, 8192^3), narrower tiles for
-    # small M, the one-CTA kernel's widths for M <= 128.
+    # small M (CTA pairs at every M, a pair's second CTA all padding at M <= 128).
     import pytest
 
     import fp4_gemm
@@ -60,7 +60,7 @@ def test_gemm_tile_width_model_decisions():
             (512, 2880, 2880): 128, (256, 2880, 2880): 128}
     got = {s: fp4_gemm.gemm_tile_width(*s) for s in want}
     assert got == want
-    assert fp4_gemm.gemm_tile_width(128, 2880, 2880) in (128, 192, 256)
-    assert fp4_gemm.gemm_tile_width(1, 8, 128) in (128, 192, 256)
+    assert fp4_gemm.gemm_tile_width(128, 2880, 2880) == 128  # the same model as M = 256: one row of pair tiles
+    assert fp4_gemm.gemm_tile_width(1, 8, 128) in (128, 192, 256, 320, 384)
     with pytest.raises(ValueError):
         fp4_gemm.gemm_tile_width(0, 128, 128)
