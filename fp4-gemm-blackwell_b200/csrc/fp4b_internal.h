@@ -48,8 +48,8 @@ struct GemmArgs {
 
 const char* gemm_check(const GemmArgs& g);
 // Output columns per tile that gemm_launch picks without FP4B_PAIR / FP4B_FORCE_BN:
-// the CTA-pair kernel's 128 / 192 / 256 / 320 / 384 for m > 128, else the
-// one-CTA kernel's 128 / 192 / 256; -1 on bad arguments.  Host only.
+// the CTA-pair kernel's 128 / 192 / 256 / 320 / 384 (pairs at every M); -1 on
+// bad arguments.  Host only.
 int gemm_tile_width(long m, long n, long k_pad, int sms);
 cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream);
 
@@ -77,8 +77,8 @@ cudaError_t quantize_units_launch(const QuantizeArgs& a, uint32_t* ready, int ri
 // GEMM whose output tile is also stored into `npeers` (1..7) other BF16
 // buffers with the same row stride (other GPUs' memory mapped into this
 // process, each offset to the columns this rank computes): the column-parallel
-// all-gather done by the epilogue.  CTA-pair path only (M > 128), no C, D rows
-// 16-byte aligned; else cudaErrorNotSupported.
+// all-gather done by the epilogue.  CTA-pair kernel, no C, D rows 16-byte
+// aligned; else cudaErrorNotSupported.
 cudaError_t gemm_launch_peers(const GemmArgs& g, void* const* peers, int npeers, cudaStream_t stream);
 
 

@@ -601,7 +601,7 @@ def gemm_prequantized(a_fp4, a_sf, m: int, b_fp4, b_sf, n: int, k_pad: int, bias
 def gemm_tile_width(m: int, n: int, k: int, sms: int = 148) -> int:
     """Output columns per tile the GEMM's time model picks for M x N x K on a
     device with `sms` SMs (no device work): 128 / 192 / 256, or the two-MMA
-    320 / 384 on CTA pairs when M > 128."""
+    320 / 384, on CTA pairs at every M."""
     w = _lib.fp4b_gemm_tile_width(m, n, k, sms)
     if w < 0:
         raise ValueError(f"gemm_tile_width: {_last_error()}")
