@@ -1652,6 +1652,7 @@ cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream) {
         case 256: return deep ? launch_tile<256, 4, 1>(g, stream, sms) : launch_tile<256, 2, 2>(g, stream, sms);
         case 192: return deep ? launch_tile<192, 4, 1>(g, stream, sms) : launch_tile<192, 2, 2>(g, stream, sms);
         case 128: return deep ? launch_tile<128, 6, 1>(g, stream, sms) : launch_tile<128, 3, 2>(g, stream, sms);
+        case 64: return deep ? launch_tile<64, 7, 1>(g, stream, sms) : launch_tile<64, 3, 2>(g, stream, sms);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -46,6 +46,23 @@ def test_tile_widths(cuda, fp4, monkeypatch, pair, bn, m, n, k):
     assert fp4.device_error() == 0
 
 
+@pytest.mark.parametrize("deep", ["1", "0"])
+@pytest.mark.parametrize("m,n,k", [(1, 8, 128), (100, 1000, 640), (300, 200, 384), (128, 2880, 2880)])
+def test_one_cta_64_wide_tile(cuda, fp4, monkeypatch, deep, m, n, k):
+    # The one-CTA kernel's 128 x 64 tile (FP4B_PAIR=0 FP4B_FORCE_BN=64; half of
+    # its tiles start 64 rows into a scale-B atom) gives the default's bytes.
+    x = W.normal_bf16((m, k), 1.0, 5 * m + n)
+    w = W.normal_bf16((n, k), 1.0, k + 1)
+    want = run_prequant(fp4, x, w)
+    monkeypatch.setenv("FP4B_PAIR", "0")
+    monkeypatch.setenv("FP4B_FORCE_BN", "64")
+    monkeypatch.setenv("FP4B_DEEP", deep)
+    d = run_prequant(fp4, x, w)
+    assert torch.equal(d, want)
+    assert_gemm_close(d, oracle_linear(x, w), f"one-CTA bn=64 {m}x{n}x{k}")
+    assert fp4.device_error() == 0
+
+
 def test_alpha_beta_c_bias(cuda, fp4):
     m, n, k = 256, 384, 512
     x = W.normal_bf16((m, k), 1.0, 1)
