@@ -637,9 +637,14 @@ constexpr int kPairEpiWarps = 8;  // two per TMEM lane quadrant, each storing ha
 // columns [0, BN), N = BN1 on [BN, BN + BN1)) share the A tile, which moves
 // fewer operand bytes per column; its accumulator is single-buffered, so it
 // suits problems whose tiles fit in one round of CTA pairs.
-template <int BN, int STAGES, int NSUB = 1, int BN1 = BN>
+// CHUNKS: 128-byte-wide chunks of K per stage (K = 256 each), loaded as one
+// TMA box per operand and chunk, back to back.  Two chunks per stage stream a
+// weight that comes from HBM (small M) faster: each weight row is read 256
+// contiguous bytes at a time instead of 128.
+template <int BN, int STAGES, int NSUB = 1, int BN1 = BN, int CHUNKS = 1>
 struct PairCfg {
-    static constexpr int kKbPerStage = 4;   // a stage covers K = 256: one 128-byte chunk
+    static constexpr int kChunks = CHUNKS;
+    static constexpr int kKbPerStage = 4 * CHUNKS;   // 64-element k-blocks per stage
     static_assert(BN % 64 == 0 && BN >= 128 && BN <= 256, "BN must be 128, 192 or 256");
     static_assert(BN1 % 64 == 0 && BN1 >= 128 && BN1 <= 256, "BN1 must be 128, 192 or 256");
     static_assert(NSUB == 1 || NSUB == 2, "one or two MMAs per k-block");
@@ -648,10 +653,12 @@ struct PairCfg {
     static constexpr int BH = BN / 2;       // B rows of the first MMA held by each CTA
     static constexpr int BH1 = BN1 / 2;     // B rows of the second MMA held by each CTA
     static constexpr int NRT = max_row_tiles(TW);
-    static constexpr int A_BYTES = kBM * kChunkBytes;
+    static constexpr int A_CHUNK = kBM * kChunkBytes;          // one TMA box of A
+    static constexpr int A_BYTES = CHUNKS * A_CHUNK;
     static constexpr int B_SUB_BYTES = BH * kChunkBytes;
     static constexpr int B_SUB1_BYTES = BH1 * kChunkBytes;
-    static constexpr int B_BYTES = B_SUB_BYTES + (NSUB - 1) * B_SUB1_BYTES;
+    static constexpr int B_CHUNK = B_SUB_BYTES + (NSUB - 1) * B_SUB1_BYTES;  // the B boxes of one chunk
+    static constexpr int B_BYTES = CHUNKS * B_CHUNK;
     static constexpr int SFA_BYTES = kKbPerStage * kAtomBytes;
     static constexpr int SFB_BYTES = NRT * kKbPerStage * kAtomBytes;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
@@ -788,14 +795,15 @@ __device__ __forceinline__ void team_epilogue_pieces(const Params& p, const CUte
     }
 }
 
-template <int BN, int STAGES, bool AWAIT, int NSUB, int BN1, bool PIECES>
+template <int BN, int STAGES, bool AWAIT, int NSUB, int BN1, bool PIECES, int CHUNKS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     nvf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_b1,
                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
                           const __grid_constant__ CUtensorMap tmap_d, const __grid_constant__ CUtensorMap tmap_d64,
                           const __grid_constant__ Params p, const __grid_constant__ PeerMaps pm) {
-    using C = PairCfg<BN, STAGES, NSUB, BN1>;
+    using C = PairCfg<BN, STAGES, NSUB, BN1, CHUNKS>;
+    static_assert(!AWAIT || CHUNKS == 1, "the quantizer's unit counters cover K stages of 256");
     constexpr int TW = C::TW;
     constexpr int TILE_M = 2 * kBM;
     constexpr int kKbPerStage = C::kKbPerStage;
@@ -930,17 +938,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 const int sub = (NSUB > 1 && role == 1 && lane == ((it + 16) & 31)) ? 1 : 0;
                 if (lane == (it & 31) || sub == 1) {
                     const uint32_t bar = full0 + (uint32_t)s * 8u;
-                    const int kx = ks * kChunkBytes;
                     const int kb0 = ks * kKbPerStage;
                     if (role == 0) {
                         if (rank == 0) ptx::mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
-                        ptx::tma_load_2d_pair(sA + s * C::A_BYTES, &tmap_a, bar, kx, a_row);
+#pragma unroll
+                        for (int c = 0; c < CHUNKS; ++c)
+                            ptx::tma_load_2d_pair(sA + s * C::A_BYTES + c * C::A_CHUNK, &tmap_a, bar,
+                                                  (ks * CHUNKS + c) * kChunkBytes, a_row);
                     } else if (role == 1) {
-                        if (sub == 0)
-                            ptx::tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_b, bar, kx, b_row);
-                        else  // the second MMA's rows [n0 + BN, n0 + TW), split between the CTAs
-                            ptx::tma_load_2d_pair(sB + s * C::B_BYTES + C::B_SUB_BYTES, &tmap_b1, bar, kx,
-                                                  n0 + BN + (int)rank * C::BH1);
+#pragma unroll
+                        for (int c = 0; c < CHUNKS; ++c) {
+                            const int kx = (ks * CHUNKS + c) * kChunkBytes;
+                            uint8_t* dst = sB + s * C::B_BYTES + c * C::B_CHUNK;
+                            if (sub == 0)
+                                ptx::tma_load_2d_pair(dst, &tmap_b, bar, kx, b_row);
+                            else  // the second MMA's rows [n0 + BN, n0 + TW), split between the CTAs
+                                ptx::tma_load_2d_pair(dst + C::B_SUB_BYTES, &tmap_b1, bar, kx,
+                                                      n0 + BN + (int)rank * C::BH1);
+                        }
                     } else if (role == 2) {
                         ptx::tma_load_3d_pair(sSFA + s * C::SFA_BYTES, &tmap_sfa, bar, 0, kb0, sfa_rt);
                     } else {
@@ -1015,11 +1030,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                                     ptx::tc_cp_32x128b_warpx4_pair(
                                         sfb_t + j * 4 * C::NRT + 4 * r,
                                         sfb_s + (uint64_t)(((r * kKbPerStage + j) * kAtomBytes) >> 4));
-                                const uint32_t koff = (uint32_t)((32 * j) >> 4);
+                                // k-block j: 32 bytes into its chunk's 128-byte rows
+                                const uint32_t koff = (uint32_t)((32 * (j & 3)) >> 4);
+                                const uint64_t a_kb = CHUNKS == 1 ? a_s : a_s + (uint64_t)(((j >> 2) * C::A_CHUNK) >> 4);
+                                const uint64_t b_kb = CHUNKS == 1 ? b_s : b_s + (uint64_t)(((j >> 2) * C::B_CHUNK) >> 4);
 #pragma unroll
                                 for (int u = 0; u < NSUB; ++u)
-                                    ptx::tc_mma_nvf4_pair(acc + u * BN, a_s + koff,
-                                                          b_s + (uint64_t)((u * C::B_SUB_BYTES) >> 4) + koff,
+                                    ptx::tc_mma_nvf4_pair(acc + u * BN, a_kb + koff,
+                                                          b_kb + (uint64_t)((u * C::B_SUB_BYTES) >> 4) + koff,
                                                           u == 0 ? idesc : idesc1, sfa_t + 4 * j,
                                                           sfb_t + j * 4 * C::NRT + shift_words + (u * BN) / 32,
                                                           (j == 0) ? first : 1u);
@@ -1413,11 +1431,11 @@ int max_pairs(K kernel, int smem, int sms, int threads) {
 // Shared memory of one SM (233472 bytes on B200) minus a CTA's reserved 1 KB.
 constexpr int kSmemPerSm = 233472;
 
-template <int BN, int STAGES, bool AWAIT = false, int NSUB = 1, int BN1 = BN, bool PIECES = false>
+template <int BN, int STAGES, bool AWAIT = false, int NSUB = 1, int BN1 = BN, bool PIECES = false, int CHUNKS = 1>
 cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, int sms, const QuantizeArgs* qa = nullptr,
                         uint32_t* ready = nullptr, void* const* peers = nullptr, int npeers = 0) {
-    using C = PairCfg<BN, STAGES, NSUB, BN1>;
-    auto kernel = nvf4_gemm_pair_kernel<BN, STAGES, AWAIT, NSUB, BN1, PIECES>;
+    using C = PairCfg<BN, STAGES, NSUB, BN1, CHUNKS>;
+    auto kernel = nvf4_gemm_pair_kernel<BN, STAGES, AWAIT, NSUB, BN1, PIECES, CHUNKS>;
     static std::once_flag attr_once[64];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1516,25 +1534,25 @@ int choose_bn(long m, long n, int sms) {
 }
 
 // Tile width of the CTA-pair kernel: the one with the smallest modelled time,
-//   rounds x (stages x stage time + per-round overhead) + fixed cost,
-// rounds = ceil(tiles / pairs), a stage = K of 256, fitted to back-to-back
-// B200 runs from 512x2880x2880 to 8192^3 (each within ~5 % of the fit).
-// BN = 128 / 192 / 256: stage time 0.30 / 0.37 / 0.44 us (the TMA ring and the
-// tensor pipe, both ~busy), per-round overhead ~1 us with two accumulators in
-// TMEM (the epilogue overlaps the next tile) and 2.1 us for BN = 256.  The
-// two-MMA tiles (one A tile shared by an N = 192 + 192 or 128 + 192 pair of
-// MMAs, a single accumulator) take nearly the same time per stage whatever
-// their width, as operand delivery sets the pace: 0.58 / 0.53 us for 384 /
-// 320 with 2.3 / 3.2 us per round (part of each exposed epilogue overlaps the
-// next tile's first loads), fitted on 8192x15360x2880, 8192^3, the headline
-// and 4096x2880x7680.  The 320-wide tile wins where it needs no more rounds,
-// e.g. 72 tiles for N = 2880 on 74 pairs; the 384-wide one on short-K
-// many-round shapes (8192x15360x2880: 170 us against 191 us with BN = 192).
+//   rounds x (stages x stage time + per-round overhead),
+// rounds = ceil(tiles / pairs), a stage = K of 256 (the fixed cost is the same
+// for every width).  Least-squares fit to back-to-back cached-linear steps on
+// B200 over 15 shapes from 256x2880x2880 to 8192x15360x2880, every width
+// (rms error 0.8 us; the pick is the measured best on 14 of them, 4.7 % off
+// on the last): stage time 0.213 / 0.221 / 0.317 / 0.350 / 0.392 us and
+// per-round overhead 0.61 / 1.23 / 1.88 / 2.72 / 2.60 us for BN = 128 / 192 /
+// 256 / 320 (= 128 + 192, two MMAs per k-block on one A tile) / 384 (= 2 x
+// 192).  The 128- and 192-wide tiles load two K chunks per stage, which makes
+// the 192-wide one the choice for most multi-round shapes with K <= 4096
+// (8192 x 5120 x 2880: 72.5 us against 79.5 with the 384-wide tile); the
+// 320-wide one wins where its tiles need no more rounds (the headline: 72
+// tiles on 74 pairs) and at long K; the 384-wide one on wide-N short-K
+// shapes (8192 x 15360 x 2880: 180.8 us against 188.3 with 192).
 // Returns 128, 192, 256, 320 (= 128 + 192) or 384 (= 2 x 192).
 int choose_bn_pair(long m, long n, long k_pad, int sms) {
-    struct Width { int code; double stage_us, round_us, fixed_us; };
-    static const Width cands[] = {{384, 0.58, 2.3, 3.0}, {320, 0.53, 3.2, 3.0}, {256, 0.44, 2.06, 5.0},
-                                  {192, 0.37, 1.0, 5.0}, {128, 0.30, 1.0, 5.0}};
+    struct Width { int code; double stage_us, round_us; };
+    static const Width cands[] = {{384, 0.392, 2.60}, {320, 0.350, 2.72}, {256, 0.317, 1.88},
+                                  {192, 0.221, 1.23}, {128, 0.213, 0.61}};
     const long mt = (m + 2 * kBM - 1) / (2 * kBM);
     const long pairs = sms / 2 > 0 ? sms / 2 : 1;
     const double stages = (double)((k_pad + 255) / 256);
@@ -1543,7 +1561,7 @@ int choose_bn_pair(long m, long n, long k_pad, int sms) {
     for (const Width& w : cands) {
         const long tiles = mt * ((n + w.code - 1) / w.code);
         const long rounds = (tiles + pairs - 1) / pairs;
-        const double cost = (double)rounds * (stages * w.stage_us + w.round_us) + w.fixed_us;
+        const double cost = (double)rounds * (stages * w.stage_us + w.round_us);
         if (best_cost < 0.0 || cost < best_cost) {
             best_cost = cost;
             best = w.code;
@@ -1593,8 +1611,8 @@ cudaError_t gemm_launch_peers(const GemmArgs& g, void* const* peers, int npeers,
     const int bn = force ? atoi(force) : choose_bn_pair(g.m, g.n_out, g.k_pad, sms);
     switch (bn) {
         case 256: return launch_pair<256, 5, false, 1, 256, true>(g, stream, sms, nullptr, nullptr, peers, npeers);
-        case 192: return launch_pair<192, 6, false, 1, 192, true>(g, stream, sms, nullptr, nullptr, peers, npeers);
-        case 128: return launch_pair<128, 7, false, 1, 128, true>(g, stream, sms, nullptr, nullptr, peers, npeers);
+        case 192: return launch_pair<192, 3, false, 1, 192, true, 2>(g, stream, sms, nullptr, nullptr, peers, npeers);
+        case 128: return launch_pair<128, 3, false, 1, 128, true, 2>(g, stream, sms, nullptr, nullptr, peers, npeers);
         case 384: return launch_pair<192, 4, false, 2, 192, true>(g, stream, sms, nullptr, nullptr, peers, npeers);
         case 320: return launch_pair<128, 4, false, 2, 192, true>(g, stream, sms, nullptr, nullptr, peers, npeers);
         default: return cudaErrorInvalidValue;
@@ -1635,10 +1653,20 @@ cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     if (pair) {
         const char* force = getenv("FP4B_FORCE_BN");
         const int bn = force ? atoi(force) : choose_bn_pair(g.m, g.n_out, g.k_pad, sms);
+        // The 128- and 192-wide tiles load two K chunks per stage (3 stages of
+        // 2 x 128-byte chunks instead of 6-7 of one: 4-15 % faster, most at small
+        // M, where the weight streams from HBM; FP4B_KCHUNKS=1 selects one).  The
+        // wider tiles keep one: two would leave them two stages (6-9 % slower).
+        const char* kc_env = getenv("FP4B_KCHUNKS");
+        const int kchunks = kc_env ? atoi(kc_env) : 2;
         switch (bn) {
             case 256: return launch_pair<256, 5, false>(g, stream, sms);
-            case 192: return launch_pair<192, 6, false>(g, stream, sms);
-            case 128: return launch_pair<128, 7, false>(g, stream, sms);
+            case 192:
+                return kchunks == 2 ? launch_pair<192, 3, false, 1, 192, false, 2>(g, stream, sms)
+                                    : launch_pair<192, 6, false>(g, stream, sms);
+            case 128:
+                return kchunks == 2 ? launch_pair<128, 3, false, 1, 128, false, 2>(g, stream, sms)
+                                    : launch_pair<128, 7, false>(g, stream, sms);
             case 384: return launch_pair<192, 4, false, 2>(g, stream, sms);
             case 320: return launch_pair<128, 4, false, 2, 192>(g, stream, sms);
             default: return cudaErrorInvalidValue;

@@ -217,3 +217,25 @@ def test_bias_add_equals_bf16_add_of_unbiased_output(cuda, fp4, monkeypatch, pai
     want = (plain.float() + b.to(plain.device).float()).to(torch.bfloat16)
     assert torch.equal(biased, want)
     assert fp4.device_error() == 0
+
+
+@pytest.mark.parametrize("bn", ["128", "192"])
+@pytest.mark.parametrize("m,n,k", [(1, 2880, 2880), (300, 1000, 640), (256, 384, 128), (2304, 3200, 2944),
+                                   (512, 2880, 7680)])
+def test_two_k_chunks_per_stage_equal_one(cuda, fp4, monkeypatch, bn, m, n, k):
+    # The 128- and 192-wide pair tiles load two 128-byte K chunks per stage by
+    # default (a K of 512 per stage; the last stage may hold 1-7 of its 8
+    # k-blocks); the MMAs run in the same K order, so the bytes equal one chunk
+    # per stage, including multi-round shapes that reuse both accumulators.
+    x = W.normal_bf16((m, k), 1.0, 3 * m + k)
+    w = W.normal_bf16((n, k), 1.0, n + 7)
+    b = W.normal_bf16((n,), 1.0, 11)
+    monkeypatch.setenv("FP4B_FORCE_BN", bn)
+    monkeypatch.setenv("FP4B_KCHUNKS", "1")
+    one = run_prequant(fp4, x, w, bias=b)
+    monkeypatch.setenv("FP4B_KCHUNKS", "2")
+    two = run_prequant(fp4, x, w, bias=b)
+    assert torch.equal(two, one)
+    if m * n * k < 2e9:
+        assert_gemm_close(two, oracle_linear(x, w, bias=b), f"2 K chunks bn={bn} {m}x{n}x{k}")
+    assert fp4.device_error() == 0

@@ -49,13 +49,14 @@ def test_global_scale_reduces_error_of_small_weights_in_the_oracle():
 def test_gemm_tile_width_model_decisions():
     # The tile width the GEMM picks from its time model (host only), for the
     # shapes it was fitted on, with B200's 148 SMs: the 320-wide two-MMA tile
-    # for the headline (72 tiles on 74 CTA pairs), the 384-wide one for
-    # short-K many-round shapes (config-5 gate_up, 8192^3), narrower tiles for
+    # for the headline (72 tiles on 74 CTA pairs), the 384-wide one for wide-N
+    # short-K shapes (config-5 gate_up) and 8192^3, the 192-wide one (two K
+    # chunks per stage) for most other multi-round shapes, narrower tiles for
     # small M (CTA pairs at every M, a pair's second CTA all padding at M <= 128).
     import pytest
 
     import fp4_gemm
-    want = {(2048, 2880, 7680): 320, (4096, 2880, 7680): 320, (8192, 15360, 2880): 384, (8192, 5120, 2880): 384,
+    want = {(2048, 2880, 7680): 320, (4096, 2880, 7680): 320, (8192, 15360, 2880): 384, (8192, 5120, 2880): 192,
             (8192, 8192, 8192): 384, (16384, 16384, 16384): 384, (2048, 5120, 2880): 192, (1024, 2880, 7680): 192,
             (512, 2880, 2880): 128, (256, 2880, 2880): 128}
     got = {s: fp4_gemm.gemm_tile_width(*s) for s in want}
