@@ -643,7 +643,6 @@ constexpr int kPairEpiWarps = 8;  // two per TMEM lane quadrant, each storing ha
 // contiguous bytes at a time instead of 128.
 template <int BN, int STAGES, int NSUB = 1, int BN1 = BN, int CHUNKS = 1>
 struct PairCfg {
-    static constexpr int kChunks = CHUNKS;
     static constexpr int kKbPerStage = 4 * CHUNKS;   // 64-element k-blocks per stage
     static_assert(BN % 64 == 0 && BN >= 128 && BN <= 256, "BN must be 128, 192 or 256");
     static_assert(BN1 % 64 == 0 && BN1 >= 128 && BN1 <= 256, "BN1 must be 128, 192 or 256");
