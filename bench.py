@@ -729,10 +729,10 @@ def run_quantize(args):
 
 
 def run_gemm(args):
-    """The headline GEMM alone (`--config gemm`): 2048 x 2880 x 7680 + bias on
-    operands quantized beforehand, buffer sets rotated past L2, one JSON line.
-    The command the GEMM's ncu captures run (one kernel per step, nothing else
-    in the timed loop)."""
+    """One GEMM alone (`--config gemm`): the headline 2048 x 2880 x 7680 + bias,
+    or `--shape MxNxK`, on operands quantized beforehand, buffer sets rotated
+    past L2, one JSON line.  The command the GEMM's ncu captures run (one kernel
+    per step, nothing else in the timed loop)."""
     import fp4_gemm
     from tests import workloads as W
 
@@ -741,12 +741,13 @@ def run_gemm(args):
     lib = fp4_gemm._lib
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
-    m, n, k = W.HEADLINE_SHAPE
+    m, n, k = tuple(int(v) for v in args.shape.split("x")) if args.shape else W.HEADLINE_SHAPE
     sets, per_set = headline_sets(m, n, k, 0, dev)
     ms = time_rotating([gemm_fn(lib, st, m, n, sptr) for st in sets], args.steps, args.warmup, stream)
     tflops = 2.0 * m * n * k / (ms * 1e-3) / 1e12
     tile = fp4_gemm.gemm_tile_width(m, n, k, torch.cuda.get_device_properties(dev).multi_processor_count)
-    print(json.dumps({"metric": "headline GEMM TFLOPS (2048x2880x7680 + bias, operands pre-quantized)",
+    what = "headline GEMM" if (m, n, k) == tuple(W.HEADLINE_SHAPE) else "GEMM"
+    print(json.dumps({"metric": f"{what} TFLOPS ({m}x{n}x{k} + bias, operands pre-quantized)",
                       "value": tflops, "unit": "TFLOPS", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
                       "ms_per_step": ms, "higher_is_better": True, "dtype": "nvfp4", "data": "synthetic",
                       "config": {"workload": f"GEMM {m}x{n}x{k} + bias, {tile}-wide CTA-pair tiles",
@@ -799,6 +800,7 @@ def main():
                          "the headline GEMM alone; fp4peak: the measured NVFP4 MMA rate (none of these is the "
                          "headline metric)")
     ap.add_argument("--layers", type=int, default=12)
+    ap.add_argument("--shape", default=None, help="--config gemm: MxNxK (default the headline 2048x2880x7680)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.config == "stack":
